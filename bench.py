@@ -1,0 +1,518 @@
+"""Benchmark of the decode-step hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-ops]
+
+Headline (one JSON line on rank 0): decode tokens/s of a full random-init Llama-1B-shaped
+decode step (16 layers, d 2048, 32/8 heads, HD 64, SwiGLU 8192, vocab
+128256, batch 32, contexts U[512, 4096]) tensor-parallel over N GPUs (strong scaling: the
+same 32 tokens per step at every N).  At N=1 the line also carries the per-op HBM GB/s of
+configs 1-4 ("ops") and the roofline of the dominant kernel.
+
+--impl reference times the reference path's CPU restatement (the NumPy float32 port in
+oracle/step.py; the reference itself is Metal/Swift and cannot run here) on the host cores,
+on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH = 32
+CTX_LO, CTX_HI = 512, 4096
+SEED_W, SEED_KV, SEED_CTX, SEED_TOK = 1234, 99, 7, 3
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
+
+
+def peaks() -> tuple[float, str]:
+    try:
+        return float(json.loads(PEAKS_FILE.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+def ctx_lens(batch=BATCH, seed=SEED_CTX):
+    return np.random.default_rng(seed).integers(CTX_LO, CTX_HI + 1, size=batch).astype(np.int32)
+
+
+def step_bytes(shape, lens, tp: int) -> float:
+    """Algorithmic HBM bytes of one decode step on ONE rank: its weight shard (fp16, norms
+    fp32), its KV heads' cached tokens (K and V fp16) and the appended token."""
+    d, hd = shape.dim, shape.head_dim
+    per_layer = (shape.qkv_dim * d + d * shape.n_heads * hd + 3 * d * shape.ffn_dim) * 2 / tp + 2 * d * 4
+    head = -(-shape.vocab // tp) * d * 2 + d * 4
+    kv = sum(int(n) + 1 for n in lens) * (shape.n_kv_heads // tp) * hd * 2 * 2 * shape.n_layers
+    return shape.n_layers * per_layer + head + kv
+
+
+# ----------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = "clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return None
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 2 + i and r[2 + i].lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(self.rows),
+        }
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline: the NumPy float32 port of the step, on a bounded sample
+# ----------------------------------------------------------------------------------------------
+
+
+class CpuBaseline:
+    """The NumPy float32 port of the config-5 step (oracle/step.py CpuDecodeF32) on a bounded
+    sample: 2 of the 16 layers (same shapes, batch 32, same context distribution) plus the
+    full LM head.  One sample's step time is estimated as 16 x (mean layer time) + LM head."""
+
+    N_SAMPLE = 2
+
+    def __init__(self):
+        from oracle import step as S
+
+        cfg = S.LLAMA_1B
+        self.cfg = cfg
+        sub = S.ModelConfig(cfg.dim, self.N_SAMPLE, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
+        w = S.synth_weights(sub, seed=SEED_W)
+        lens = ctx_lens()
+        need = [-(-(int(n) + 2) // 16) for n in lens]
+        nblk = sum(need)
+        table = np.full((BATCH, -(-(CTX_HI + 2) // 16)), -1, np.int32)
+        perm = np.random.default_rng(5).permutation(nblk)
+        o = 0
+        for b, k in enumerate(need):
+            table[b, :k] = perm[o : o + k]
+            o += k
+        r = np.random.default_rng(SEED_KV)
+        shp = (nblk, cfg.n_kv_heads, 16, cfg.head_dim)
+        kp = [r.standard_normal(shp, dtype=np.float32).astype(np.float16) for _ in range(self.N_SAMPLE)]
+        vp = [r.standard_normal(shp, dtype=np.float32).astype(np.float16) for _ in range(self.N_SAMPLE)]
+        self.cd = S.CpuDecodeF32(sub, w, kp, vp, table, lens)
+        self.tokens = np.random.default_rng(SEED_TOK).integers(0, cfg.vocab, size=BATCH)
+        self.sample = (
+            f"NumPy float32 port of the config-5 step: {self.N_SAMPLE} of {cfg.n_layers} layers + full LM head "
+            f"at batch {BATCH}, ctx U[{CTX_LO},{CTX_HI}] (seed {SEED_CTX}); step time = "
+            f"{cfg.n_layers} x mean layer time + LM head"
+        )
+
+    def step_seconds(self) -> float:
+        x = self.cd.embed(self.tokens)
+        t0 = time.perf_counter()
+        for i in range(self.N_SAMPLE):
+            x = self.cd.layer(i, x)
+        t1 = time.perf_counter()
+        self.cd.lm_head(x)
+        t2 = time.perf_counter()
+        return self.cfg.n_layers * (t1 - t0) / self.N_SAMPLE + (t2 - t1)
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n and n[0]:
+            return int(n[0])
+    except Exception:
+        pass
+    return len(os.sched_getaffinity(0))
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    t0 = time.perf_counter()
+    cb = CpuBaseline()
+    for _ in range(args.warmup):
+        cb.step_seconds()
+    secs = [cb.step_seconds() for _ in range(args.steps)]
+    ms = 1000.0 * statistics.median(secs)
+    v = BATCH / (ms / 1e3)
+    print(
+        json.dumps(
+            {
+                "impl": "reference",
+                "metric": "decode tokens/s (random-init Llama-1B shape, batch 32, ctx U[512,4096], TP over n_gpus)",
+                "value": v,
+                "unit": "tokens/s",
+                "n_gpus": args.gpus,
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": ms,
+                "higher_is_better": True,
+                "scaling": "strong",
+                "vs_baseline": None,
+                "dtype": "f32",
+                "data": "synthetic (seeded random-init weights and KV contents)",
+                "config": {"workload": "config 5: Llama-1B-shape decode step, batch 32, ctx U[512,4096]", "batch": BATCH},
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port", "sample": cb.sample},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "wall_s": time.perf_counter() - t0,
+            }
+        ),
+        flush=True,
+    )
+
+
+# ----------------------------------------------------------------------------------------------
+# per-op microbenchmarks (configs 1-4) on one GPU
+# ----------------------------------------------------------------------------------------------
+
+
+def time_launches(fn, n_iter: int, stream) -> float:
+    """Average ms per call of fn(i) over n_iter calls, CUDA events on `stream`."""
+    import torch
+
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n_iter):
+        fn(i)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / n_iter
+
+
+def op_benchmarks(peak: float) -> dict:
+    import torch
+
+    from gemmagemini4hackathon2026_10_2425_b200 import ops
+    from oracle import ops as O
+
+    dev = "cuda"
+    s = torch.cuda.current_stream()
+    res = {}
+    L2 = 126 * 2**20
+
+    def copies(nbytes):  # enough distinct operand copies to exceed 2x L2
+        return max(1, -(-(2 * L2) // nbytes))
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    # config 1: fp32 2048x2048
+    M = K = 2048
+    n = copies(M * K * 4)
+    Ws = [torch.randn(M, K, generator=g, device=dev) * 0.02 for _ in range(n)]
+    x = torch.randn(K, generator=g, device=dev)
+    y = torch.empty(M, device=dev)
+    ms = time_launches(lambda i: ops.gemv_f32(Ws[i % n], x, y), 200, s)
+    b = M * K * 4 + K * 4 + M * 4
+    res["c1_f32_2048x2048"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+    del Ws
+    # config 2: fp16 with fused RMSNorm
+    for (K, M) in [(2048, 2048), (2048, 16384), (16384, 2048), (2048, 256000)]:
+        n = copies(M * K * 2)
+        Ws = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for _ in range(n)]
+        x = torch.randn(1, K, generator=g, device=dev)
+        gm = 1 + 0.1 * torch.randn(K, generator=g, device=dev)
+        y = torch.empty(1, M, device=dev)
+        ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), 50 if M > 100000 else 200, s)
+        b = M * K * 2 + K * 4 + K * 4 + M * 4
+        res[f"c2_f16_{K}to{M}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+        del Ws
+    # config 3: q8 / q4, batch 1 and 16
+    for fmt in ("q8", "q4"):
+        for (K, M) in [(4096, 4096), (4096, 14336)]:
+            wbytes = M * K * (1 if fmt == "q8" else 0.5) + M * K // 32 * 2
+            n = copies(int(wbytes))
+            Wq = []
+            for _ in range(n):
+                if fmt == "q8":
+                    q = torch.randint(-127, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+                else:
+                    q = torch.randint(0, 256, (M, K // 2), generator=g, device=dev, dtype=torch.uint8)
+                sc = (torch.randn(M, K // 32, generator=g, device=dev) * 0.01).abs().half()
+                Wq.append(ops.QWeight(fmt, q, sc))
+            for bsz in (1, 16):
+                x = torch.randn(bsz, K, generator=g, device=dev).half()
+                y = torch.empty(bsz, M, device=dev)
+                ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), 100, s)
+                b = wbytes + bsz * K * 2 + bsz * M * 4
+                res[f"c3_{fmt}_{K}to{M}_b{bsz}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+            del Wq
+    # config 4: ragged paged attention
+    r = np.random.default_rng(4)
+    B, hq, hk, hd = 64, 32, 8, 128
+    lens = r.integers(128, 8193, size=B).astype(np.int32)
+    max_ctx = 8193
+    need = [-(-(int(c) + 1) // 16) for c in lens]
+    nblk = sum(need)
+    table = np.full((B, -(-max_ctx // 16)), -1, np.int32)
+    perm = r.permutation(nblk)
+    o = 0
+    for bb, k in enumerate(need):
+        table[bb, :k] = perm[o : o + k]
+        o += k
+    kp = torch.randn(nblk, hk, 16, hd, generator=g, device=dev).half()
+    vp = torch.randn(nblk, hk, 16, hd, generator=g, device=dev).half()
+    qkv = torch.randn(B, (hq + 2 * hk) * hd, generator=g, device=dev).half()
+    tb, ln = torch.from_numpy(table).to(dev), torch.from_numpy(lens).to(dev)
+    invf = torch.from_numpy(O.inv_freq(hd, 10000.0)).to(dev)
+    out = torch.empty(B, hq * hd, device=dev)
+    ms = time_launches(
+        lambda i: ops.paged_decode_attn(qkv, kp, vp, tb, ln, invf, hq, hk, hd, max_ctx, out=out), 50, s
+    )
+    tot = int((lens + 1).sum())
+    b = tot * hk * hd * 2 * 2 + B * (hq + 2 * hk) * hd * 2 + B * hq * hd * 4 + 4 * sum(need) + B * hk * hd * 2 * 2
+    res["c4_paged_attn_64seq"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+    return res
+
+
+# ----------------------------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------------------------
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from gemmagemini4hackathon2026_10_2425_b200 import _lib, ops
+    from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, make_block_table, share_nccl_id
+    from gemmagemini4hackathon2026_10_2425_b200.tp import LLAMA_1B
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    _lib.lib()
+
+    shape = LLAMA_1B
+    lens = ctx_lens()
+    steps_total = args.warmup + args.steps
+    headroom = 2 * steps_total + 4  # e2e loop advances every context by one token per step
+    max_ctx = int(lens.max()) + headroom + 16
+    max_blocks = -(-max_ctx // 16)
+    n_blocks = sum(-(-(int(c) + headroom) // 16) for c in lens) + 8
+    nccl_id = share_nccl_id(rank) if world > 1 else None
+    eng = DecodeEngine(shape, max_batch=BATCH, max_ctx=max_ctx, n_blocks=n_blocks, tp_rank=rank, tp_size=world, nccl_id=nccl_id, device=dev)
+    eng.alloc_kv(fill_seed=SEED_KV)
+    eng.random_weights(SEED_W)
+    table = make_block_table(lens, max_blocks, n_blocks, seed=5, headroom=headroom).to(dev)
+    tokens0 = np.random.default_rng(SEED_TOK).integers(0, shape.vocab, size=BATCH).astype(np.int32)
+    tok_d = torch.from_numpy(tokens0).to(dev)
+    ctx_d = torch.from_numpy(lens.copy()).to(dev)
+    nxt_d = torch.empty_like(tok_d)
+    s = eng.stream
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident loop: same inputs every step (fixed contexts), graph replay
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            eng.step(tok_d, ctx_d, table, nxt_d)
+    n0 = _lib.lib().b2d_launch_counter()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        time.sleep(0.3)
+        e0.record(s)
+        for _ in range(args.steps):
+            eng.step(tok_d, ctx_d, table, nxt_d)
+        e1.record(s)
+        e1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    # launches per step: capture-time count of a fresh graph (launch counter is per thread)
+    c0 = _lib.lib().b2d_launch_counter()
+    with torch.cuda.stream(s):
+        eng.step(tok_d, ctx_d, table, nxt_d, use_graph=False)
+    torch.cuda.synchronize()
+    launches_per_step = _lib.lib().b2d_launch_counter() - c0
+
+    # ---- end-to-end through the public API: host tokens in, host tokens out, every step
+    tok_h = torch.from_numpy(tokens0.copy()).pin_memory()
+    ctx_h = torch.from_numpy(lens.copy()).pin_memory()
+    nxt_h = torch.empty(BATCH, dtype=torch.int32).pin_memory()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+
+    def e2e_step():
+        with torch.cuda.stream(s):
+            tok_d.copy_(tok_h, non_blocking=True)
+            ctx_d.copy_(ctx_h, non_blocking=True)
+            eng.step(tok_d, ctx_d, table, nxt_d)
+            nxt_h.copy_(nxt_d, non_blocking=True)
+        s.synchronize()
+        tok_h.copy_(nxt_h)
+        ctx_h.add_(1)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    ctx_h.copy_(torch.from_numpy(lens + args.warmup))
+    barrier()
+    torch.cuda.synchronize()
+    e2.record(s)
+    for _ in range(args.steps):
+        e2e_step()
+    e3.record(s)
+    e3.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3)) / args.steps
+
+    peak, peak_kind = peaks()
+    out = {
+        "metric": "decode tokens/s (random-init Llama-1B shape, batch 32, ctx U[512,4096], TP over n_gpus)",
+        "value": BATCH / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded random-init fp16 weights ~N(0,0.02), fp16 KV contents ~N(0,1))",
+        "config": {
+            "workload": "config 5: Llama-1B-shape decode step (16 layers, d2048, 32/8 heads, HD64, FFN 8192, vocab 128256)",
+            "batch": BATCH,
+            "ctx": f"U[{CTX_LO},{CTX_HI}] seed {SEED_CTX}",
+            "parallelism": f"tp{world}",
+            "l2": "per-step operands (weights + KV, GBs) exceed the 126 MB L2; no flush needed",
+        },
+        "hbm_gbs_per_gpu": step_bytes(shape, lens, world) / (ms / 1e3) / 1e9,
+        "hbm_frac_per_gpu": step_bytes(shape, lens, world) / (ms / 1e3) / 1e9 / peak,
+        "e2e": {
+            "value": BATCH / (ms_e2e / 1e3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": 2 * BATCH * 4,
+            "d2h_bytes_per_step": BATCH * 4,
+            "note": "greedy decode loop through DecodeEngine.step: pinned-host tokens + positions in, next tokens out, host sync every step; contexts advance one token per step",
+        },
+        "gpu_launches": int(launches_per_step * args.steps),
+        "clocks": clk.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_ops:
+        res = op_benchmarks(peak)
+        out["ops"] = res
+        # dominant kernel of the step: gate/up SwiGLU GEMV (batch 32) over the 16 layers' weights
+        L0 = eng.layers
+        x = torch.randn(BATCH, shape.dim, device=dev)
+        gm = torch.ones(shape.dim, device=dev)
+        h = torch.empty(BATCH, shape.ffn_dim // world, device=dev)
+        ms_k = time_launches(
+            lambda i: ops.gemv(L0[i % len(L0)]["wgate"], x, gamma=gm, eps=1e-5, epilogue="swiglu", W_up=L0[i % len(L0)]["wup"], y=h),
+            64,
+            torch.cuda.current_stream(),
+        )
+        kb = 2 * shape.ffn_dim * shape.dim * 2 + BATCH * shape.dim * 4 + BATCH * shape.ffn_dim * 4
+        out["roofline"] = {
+            "kernel": "gemv_kernel<F16, swiglu> (gate/up, batch 32 as 4 launches of 8 rows)",
+            "bound": "hbm",
+            "achieved": kb / ms_k / 1e6,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": kb / ms_k / 1e6 / peak,
+            "traffic": None,
+            "bytes_per_call": kb,
+            "us_per_call": ms_k * 1e3,
+        }
+        cb = CpuBaseline()
+        cb.step_seconds()
+        t_cpu = min(cb.step_seconds() for _ in range(2))
+        out["cpu_baseline"] = {"value": BATCH / t_cpu, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port", "sample": cb.sample}
+    eng.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op (configs 1-4) microbenchmarks")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

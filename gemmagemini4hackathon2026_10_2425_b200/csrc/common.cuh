@@ -1,0 +1,112 @@
+// Shared device helpers and host-side status plumbing for the decode-step library.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200dec.h"
+
+namespace b2d {
+
+// ------------------------------------------------------------------------------------------
+// host: status handling
+// ------------------------------------------------------------------------------------------
+void set_cuda_error(cudaError_t e);
+
+// Kernel launches this library has enqueued on the calling thread (captured ones included).
+void count_launch(int n = 1);
+
+// Checks the launch that was just issued; returns B2D_OK or B2D_ERR_CUDA.
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return B2D_ERR_CUDA;
+  }
+  count_launch();
+  return B2D_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int num_sms();  // cached per device
+
+#define B2D_TRY(expr)              \
+  do {                             \
+    int _st = (expr);              \
+    if (_st != B2D_OK) return _st; \
+  } while (0)
+
+// ------------------------------------------------------------------------------------------
+// device: loads
+// ------------------------------------------------------------------------------------------
+
+// 16-byte streaming load of read-only data, not kept in L1 (weights, KV pages).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float2 h2f2(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+
+__device__ __forceinline__ float h2f(uint16_t u) { return __half2float(__ushort_as_half(u)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// Signed bytes -> floats without I2F: place byte^0x80 under the exponent of 2^23 and subtract
+// (2^23 + 128).  Exact for every int8 value.
+__device__ __forceinline__ float byte_to_float(uint32_t biased_word, int i) {
+  // biased_word already holds (word ^ 0x80808080); byte i goes to the low 8 bits
+  uint32_t f = __byte_perm(biased_word, 0x4B000000u, 0x7650 + i) ;
+  return __uint_as_float(f) - 8388736.0f;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// (value, index) max with ties to the lowest index (LK/kernels.metal:326).
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+// Programmatic dependent launch: wait for the preceding kernel's writes / let the next kernel
+// start its prologue.  Both are no-ops when the launch did not opt in.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+}  // namespace b2d

@@ -1,0 +1,344 @@
+// Decode step of a Llama-style model over a ragged paged batch, optionally tensor-parallel.
+//
+// Replaces Engine.encodeDecode (LK/main.swift:321-347): embed -> per layer [RMSNorm + QKV
+// matvec, RoPE + KV write, attention, O matvec + residual, RMSNorm + gate/up SwiGLU, down +
+// residual] -> final norm + LM head + argmax.  The reference encodes ~115 dispatches per token
+// for one sequence; here one step serves a whole batch and every RMSNorm, the RoPE, the KV
+// append and the argmax are fused into the kernel that consumes them:
+//
+//   embed                                   (1 launch)
+//   per layer: rmsnorm+QKV GEMV -> rope+append+split-K attention -> O GEMV (+residual)
+//              -> rmsnorm+gate/up SwiGLU GEMV -> down GEMV (+residual)        (5 launches)
+//   rmsnorm + LM-head GEMV + argmax         (1 launch)
+//
+// Tensor parallelism (tp > 1, one process per GPU): QKV and gate/up are column-parallel (this
+// rank's heads / FFN rows), O and down are row-parallel and their partial sums are summed
+// with ncclAllReduce before the residual add; the LM head is vocab-parallel and each rank's
+// (max, index) pair is all-gathered and combined (ties -> lowest index).  The whole step can
+// be captured once into a CUDA graph and replayed.
+#include <nccl.h>
+
+#include <cmath>
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+namespace b2d {
+int gemv_dispatch(int, const void*, const void*, const void*, const void*, int, const void*, int,
+                  const float*, float, int, int, void*, int, const float*, int, int, int,
+                  cudaStream_t);
+size_t lm_head_argmax_workspace_bytes(int V, int batch);
+int lm_head_argmax(const uint16_t*, const float*, int, const float*, float, int, int, int, int,
+                   float*, int*, float*, void*, size_t, cudaStream_t);
+int embed_f16(const uint16_t*, const int*, float*, int, int, cudaStream_t);
+int argmax_combine(const float*, const int*, int, int, int*, cudaStream_t);
+int add_f32(float*, const float*, size_t, cudaStream_t);
+size_t paged_attn_workspace_bytes(int, int, int, int, int);
+int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
+                      const float*, int, int, int, int, int, float, int, int, void*, int, int,
+                      void*, size_t, cudaStream_t);
+}  // namespace b2d
+
+using namespace b2d;
+
+struct Layer {
+  const float* attn_norm = nullptr;
+  const uint16_t* wqkv = nullptr;
+  const uint16_t* wo = nullptr;
+  const float* ffn_norm = nullptr;
+  const uint16_t* wgate = nullptr;
+  const uint16_t* wup = nullptr;
+  const uint16_t* wdown = nullptr;
+  uint16_t* k_pages = nullptr;
+  uint16_t* v_pages = nullptr;
+};
+
+struct GraphKey {
+  int batch = -1;
+  const void* ptrs[6] = {};
+  cudaStream_t stream = nullptr;
+  bool operator==(const GraphKey& o) const {
+    if (batch != o.batch || stream != o.stream) return false;
+    for (int i = 0; i < 6; ++i)
+      if (ptrs[i] != o.ptrs[i]) return false;
+    return true;
+  }
+};
+
+struct b2d_decoder {
+  b2d_model_config cfg{};
+  int rank = 0, tp = 1, device = 0;
+  ncclComm_t comm = nullptr;
+  int hq = 0, hk = 0, fl = 0, qkv_l = 0, lm_rows = 0, lm_stride = 0;
+  std::vector<Layer> layers;
+  const uint16_t* embed = nullptr;
+  const uint16_t* lm_head = nullptr;
+  const float* final_norm = nullptr;
+  // handle-owned device buffers (one allocation)
+  void* arena = nullptr;
+  float* x = nullptr;       // [B, D] residual stream, fp32
+  float* qkv = nullptr;     // [B, qkv_l]
+  float* att = nullptr;     // [B, hq*HD]
+  float* hid = nullptr;     // [B, fl]
+  float* part = nullptr;    // [B, D] row-parallel partial (tp > 1)
+  float* invf = nullptr;    // [HD/2]
+  float* cand_val = nullptr;  // [tp, B]
+  int* cand_idx = nullptr;    // [tp, B]
+  float* my_val = nullptr;    // [B]
+  int* my_idx = nullptr;      // [B]
+  void* attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+  void* am_ws = nullptr;
+  size_t am_ws_bytes = 0;
+  // graph cache
+  cudaGraphExec_t gexec = nullptr;
+  GraphKey gkey;
+};
+
+static int nccl_status(ncclResult_t r) { return r == ncclSuccess ? B2D_OK : B2D_ERR_NCCL; }
+
+static int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return B2D_OK;
+  set_cuda_error(e);
+  return B2D_ERR_CUDA;
+}
+
+static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// Enqueue one decode step on `s` (no synchronization, graph-capturable).
+static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
+                        const int* block_table, int B, int* next_tokens, float* logits,
+                        cudaStream_t s) {
+  const b2d_model_config& c = h->cfg;
+  const int D = c.dim, HD = c.head_dim;
+  const bool tpar = h->tp > 1;
+  B2D_TRY(embed_f16(h->embed, tokens, h->x, D, B, s));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Layer& L = h->layers[l];
+    // RMSNorm + QKV (column-parallel: this rank's heads)
+    B2D_TRY(gemv_dispatch(B2D_F16, L.wqkv, nullptr, nullptr, nullptr, B2D_F32, h->x, D,
+                          L.attn_norm, c.eps, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l, nullptr,
+                          h->qkv_l, D, B, s));
+    // RoPE + KV append + split-K GQA attention over the paged cache
+    B2D_TRY(paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
+                              c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
+                              c.max_ctx, 0.f, 0, 1, h->att, B2D_F32, h->hq * HD, h->attn_ws,
+                              h->attn_ws_bytes, s));
+    // O projection (row-parallel) + residual
+    if (!tpar) {
+      B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
+                            h->hq * HD, nullptr, 0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
+                            h->hq * HD, B, s));
+    } else {
+      B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
+                            h->hq * HD, nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->part, D,
+                            nullptr, D, h->hq * HD, B, s));
+      B2D_TRY(nccl_status(
+          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
+      B2D_TRY(add_f32(h->x, h->part, (size_t)B * D, s));
+    }
+    // RMSNorm + gate/up SwiGLU (column-parallel: this rank's FFN rows)
+    B2D_TRY(gemv_dispatch(B2D_F16, L.wgate, nullptr, L.wup, nullptr, B2D_F32, h->x, D,
+                          L.ffn_norm, c.eps, B2D_EPI_SWIGLU, B2D_F32, h->hid, h->fl, nullptr,
+                          h->fl, D, B, s));
+    // down projection (row-parallel) + residual
+    if (!tpar) {
+      B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
+                            nullptr, 0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D, h->fl, B,
+                            s));
+    } else {
+      B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
+                            nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->part, D, nullptr, D, h->fl,
+                            B, s));
+      B2D_TRY(nccl_status(
+          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
+      B2D_TRY(add_f32(h->x, h->part, (size_t)B * D, s));
+    }
+  }
+  // final RMSNorm + LM head (vocab-parallel) + argmax
+  const int offset = h->rank * h->lm_stride;  // first vocab row of this rank
+  if (!tpar) {
+    B2D_TRY(lm_head_argmax(h->lm_head, h->x, D, h->final_norm, c.eps, h->lm_rows, D, B, 0,
+                           logits, next_tokens, nullptr, h->am_ws, h->am_ws_bytes, s));
+  } else {
+    B2D_TRY(lm_head_argmax(h->lm_head, h->x, D, h->final_norm, c.eps, h->lm_rows, D, B, offset,
+                           logits, h->my_idx, h->my_val, h->am_ws, h->am_ws_bytes, s));
+    B2D_TRY(nccl_status(ncclGroupStart()));
+    B2D_TRY(nccl_status(ncclAllGather(h->my_val, h->cand_val, B, ncclFloat, h->comm, s)));
+    B2D_TRY(nccl_status(ncclAllGather(h->my_idx, h->cand_idx, B, ncclInt32, h->comm, s)));
+    B2D_TRY(nccl_status(ncclGroupEnd()));
+    B2D_TRY(argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s));
+  }
+  return B2D_OK;
+}
+
+extern "C" {
+
+int b2d_nccl_unique_id_bytes(void) { return (int)sizeof(ncclUniqueId); }
+
+int b2d_nccl_get_unique_id(void* out_host) {
+  if (!out_host) return B2D_ERR_NULL;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return B2D_ERR_NCCL;
+  memcpy(out_host, &id, sizeof(id));
+  return B2D_OK;
+}
+
+int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
+                       const void* nccl_id, b2d_decoder** out) {
+  if (!cfg || !out) return B2D_ERR_NULL;
+  *out = nullptr;
+  const b2d_model_config& c = *cfg;
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return B2D_ERR_SHAPE;
+  if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.head_dim <= 0 ||
+      c.ffn_dim <= 0 || c.vocab <= 0 || c.max_batch <= 0 || c.max_ctx <= 0 ||
+      c.max_blocks * 16 < c.max_ctx || c.n_blocks <= 0)
+    return B2D_ERR_SHAPE;
+  if (c.n_kv_heads % tp_size || c.n_heads % c.n_kv_heads || c.ffn_dim % tp_size)
+    return B2D_ERR_SHAPE;
+  if (tp_size > 1 && !nccl_id) return B2D_ERR_NULL;
+  b2d_decoder* h = new b2d_decoder();
+  h->cfg = c;
+  h->rank = tp_rank;
+  h->tp = tp_size;
+  cudaGetDevice(&h->device);
+  h->hq = c.n_heads / tp_size;
+  h->hk = c.n_kv_heads / tp_size;
+  h->fl = c.ffn_dim / tp_size;
+  h->qkv_l = (h->hq + 2 * h->hk) * c.head_dim;
+  h->lm_stride = (c.vocab + tp_size - 1) / tp_size;
+  h->lm_rows = std::min(h->lm_stride, c.vocab - tp_rank * h->lm_stride);
+  if (h->lm_rows <= 0) {
+    delete h;
+    return B2D_ERR_SHAPE;
+  }
+  h->layers.resize(c.n_layers);
+  const int B = c.max_batch, D = c.dim;
+  h->attn_ws_bytes =
+      paged_attn_workspace_bytes(B, h->hq, h->hk, c.head_dim, c.max_ctx);
+  h->am_ws_bytes = lm_head_argmax_workspace_bytes(h->lm_rows, B);
+  size_t sizes[] = {
+      (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,
+      (size_t)B * h->fl * 4,      (size_t)B * D * 4,        (size_t)c.head_dim / 2 * 4,
+      (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)B * 4,
+      (size_t)B * 4,              h->attn_ws_bytes,         h->am_ws_bytes};
+  size_t total = 0;
+  for (size_t s : sizes) total += align256(s);
+  int st = cuda_status(cudaMalloc(&h->arena, total));
+  if (st != B2D_OK) {
+    delete h;
+    return st;
+  }
+  cudaMemset(h->arena, 0, total);
+  char* p = static_cast<char*>(h->arena);
+  void** slots[] = {(void**)&h->x,        (void**)&h->qkv,      (void**)&h->att,
+                    (void**)&h->hid,      (void**)&h->part,     (void**)&h->invf,
+                    (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->my_val,
+                    (void**)&h->my_idx,   (void**)&h->attn_ws,  (void**)&h->am_ws};
+  for (int i = 0; i < 12; ++i) {
+    *slots[i] = p;
+    p += align256(sizes[i]);
+  }
+  std::vector<float> invf(c.head_dim / 2);
+  for (int i = 0; i < c.head_dim / 2; ++i)
+    invf[i] = (float)(1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)c.head_dim));
+  st = cuda_status(cudaMemcpy(h->invf, invf.data(), invf.size() * 4, cudaMemcpyHostToDevice));
+  if (st == B2D_OK && tp_size > 1) {
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    if (ncclCommInitRank(&h->comm, tp_size, id, tp_rank) != ncclSuccess) st = B2D_ERR_NCCL;
+  }
+  if (st != B2D_OK) {
+    cudaFree(h->arena);
+    delete h;
+    return st;
+  }
+  *out = h;
+  return B2D_OK;
+}
+
+int b2d_decoder_destroy(b2d_decoder* h) {
+  if (!h) return B2D_OK;
+  if (h->gexec) cudaGraphExecDestroy(h->gexec);
+  if (h->comm) ncclCommDestroy(h->comm);
+  if (h->arena) cudaFree(h->arena);
+  delete h;
+  return B2D_OK;
+}
+
+int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,
+                          const uint16_t* wqkv, const uint16_t* wo, const float* ffn_norm,
+                          const uint16_t* wgate, const uint16_t* wup, const uint16_t* wdown,
+                          uint16_t* k_pages, uint16_t* v_pages) {
+  if (!h) return B2D_ERR_NULL;
+  if (layer < 0 || layer >= h->cfg.n_layers) return B2D_ERR_SHAPE;
+  if (!attn_norm || !wqkv || !wo || !ffn_norm || !wgate || !wup || !wdown || !k_pages || !v_pages)
+    return B2D_ERR_NULL;
+  Layer& L = h->layers[layer];
+  L = Layer{attn_norm, wqkv, wo, ffn_norm, wgate, wup, wdown, k_pages, v_pages};
+  if (h->gexec) {  // pointers changed: the captured graph is stale
+    cudaGraphExecDestroy(h->gexec);
+    h->gexec = nullptr;
+    h->gkey = GraphKey();
+  }
+  return B2D_OK;
+}
+
+int b2d_decoder_set_head(b2d_decoder* h, const uint16_t* embed, const uint16_t* lm_head,
+                         int lm_rows, const float* final_norm) {
+  if (!h) return B2D_ERR_NULL;
+  if (!embed || !lm_head || !final_norm) return B2D_ERR_NULL;
+  if (lm_rows != h->lm_rows) return B2D_ERR_SHAPE;
+  h->embed = embed;
+  h->lm_head = lm_head;
+  h->final_norm = final_norm;
+  if (h->gexec) {
+    cudaGraphExecDestroy(h->gexec);
+    h->gexec = nullptr;
+    h->gkey = GraphKey();
+  }
+  return B2D_OK;
+}
+
+int b2d_decoder_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
+                     const int* block_table, int batch, int* next_tokens, float* logits,
+                     int use_graph, b2d_stream_t stream) {
+  if (!h) return B2D_ERR_NULL;
+  if (!tokens || !ctx_lens || !block_table || !next_tokens) return B2D_ERR_NULL;
+  if (batch <= 0 || batch > h->cfg.max_batch) return B2D_ERR_SHAPE;
+  if (!h->embed) return B2D_ERR_STATE;
+  for (const Layer& L : h->layers)
+    if (!L.wqkv) return B2D_ERR_STATE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!use_graph) return enqueue_step(h, tokens, ctx_lens, block_table, batch, next_tokens, logits, s);
+  if (s == nullptr) return B2D_ERR_STATE;  // the legacy default stream cannot be captured
+  GraphKey key;
+  key.batch = batch;
+  key.stream = s;
+  const void* ptrs[6] = {tokens, ctx_lens, block_table, next_tokens, logits, nullptr};
+  for (int i = 0; i < 6; ++i) key.ptrs[i] = ptrs[i];
+  if (!h->gexec || !(key == h->gkey)) {
+    if (h->gexec) {
+      cudaGraphExecDestroy(h->gexec);
+      h->gexec = nullptr;
+    }
+    B2D_TRY(cuda_status(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)));
+    int st = enqueue_step(h, tokens, ctx_lens, block_table, batch, next_tokens, logits, s);
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &graph);
+    if (st != B2D_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    B2D_TRY(cuda_status(e));
+    e = cudaGraphInstantiate(&h->gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    B2D_TRY(cuda_status(e));
+    h->gkey = key;
+  }
+  return cuda_status(cudaGraphLaunch(h->gexec, s));
+}
+
+}  // extern "C"

@@ -1,0 +1,248 @@
+"""DecodeEngine: host side of the decode step (the reference's Swift Engine, LK/main.swift:152-391).
+
+Owns, per rank: the sharded fp16 weights, the paged KV pools, and a b2d_decoder handle from
+libb200dec.so that runs the whole step (optionally captured in a CUDA graph).  Tensor
+parallelism uses one process per GPU; the NCCL unique id travels over torch.distributed.
+
+Weights are named like the reference's weights file (LK/convert_weights.py:60-72): embed,
+l{i}.attn_norm, l{i}.wqkv, l{i}.wo, l{i}.ffn_norm, l{i}.wgate, l{i}.wup, l{i}.wdown, final_norm;
+the LM head is tied to embed (LK/main.swift:306).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib, tp as tpmod
+from ._lib import call
+from .tp import ModelShape
+
+PAGE = 16
+
+
+def nccl_unique_id() -> bytes:
+    n = _lib.lib().b2d_nccl_unique_id_bytes()
+    buf = ctypes.create_string_buffer(n)
+    call("b2d_nccl_get_unique_id", ctypes.addressof(buf))
+    return buf.raw
+
+
+def share_nccl_id(rank: int) -> bytes:
+    """Rank 0 makes the id; every rank of the default torch.distributed group receives it."""
+    import torch.distributed as dist
+
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return obj[0]
+
+
+class DecodeEngine:
+    """A Llama-style decoder for one rank of `tp_size` (tp_size 1 = single GPU)."""
+
+    def __init__(
+        self,
+        shape: ModelShape,
+        *,
+        max_batch: int,
+        max_ctx: int,
+        n_blocks: int,
+        tp_rank: int = 0,
+        tp_size: int = 1,
+        nccl_id: bytes | None = None,
+        device: torch.device | None = None,
+    ):
+        tpmod.check_tp(shape, tp_size)
+        self.shape, self.rank, self.tp = shape, tp_rank, tp_size
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.max_batch, self.max_ctx, self.n_blocks = max_batch, max_ctx, n_blocks
+        self.max_blocks = -(-max_ctx // PAGE)
+        self.hq, self.hk = shape.n_heads // tp_size, shape.n_kv_heads // tp_size
+        cfg = _lib.ModelConfig(
+            shape.dim,
+            shape.n_layers,
+            shape.n_heads,
+            shape.n_kv_heads,
+            shape.head_dim,
+            shape.ffn_dim,
+            shape.vocab,
+            shape.eps,
+            shape.theta,
+            max_batch,
+            max_ctx,
+            self.max_blocks,
+            n_blocks,
+        )
+        self._h = ctypes.c_void_p()
+        idbuf = None
+        if tp_size > 1:
+            if nccl_id is None:
+                raise ValueError("tp_size > 1 needs the NCCL unique id from rank 0")
+            idbuf = ctypes.create_string_buffer(nccl_id, len(nccl_id))
+        with torch.cuda.device(self.device):
+            call(
+                "b2d_decoder_create",
+                ctypes.byref(cfg),
+                tp_rank,
+                tp_size,
+                ctypes.addressof(idbuf) if idbuf is not None else None,
+                ctypes.byref(self._h),
+            )
+        self.lm_rows = tpmod.vocab_rows(shape, tp_rank, tp_size)[1] - tpmod.vocab_rows(shape, tp_rank, tp_size)[0]
+        self.layers: list[dict[str, torch.Tensor]] = []
+        self.k_pages: list[torch.Tensor] = []
+        self.v_pages: list[torch.Tensor] = []
+        self.stream = torch.cuda.Stream(device=self.device)
+
+    # -- setup ------------------------------------------------------------------------------
+
+    def alloc_kv(self, fill_seed: int | None = None) -> None:
+        """Allocate this rank's page pools: per layer K and V [n_blocks, Hkv/tp, 16, HD] fp16.
+        With fill_seed, fill them with seeded N(0, 1) values (synthetic cache contents)."""
+        s = self.shape
+        shp = (self.n_blocks, self.hk, PAGE, s.head_dim)
+        g = torch.Generator(device=self.device)
+        if fill_seed is not None:
+            g.manual_seed(fill_seed + 7919 * self.rank)
+        self.k_pages, self.v_pages = [], []
+        for _ in range(s.n_layers):
+            if fill_seed is None:
+                k = torch.zeros(shp, dtype=torch.float16, device=self.device)
+                v = torch.zeros(shp, dtype=torch.float16, device=self.device)
+            else:
+                k = torch.randn(shp, generator=g, dtype=torch.float16, device=self.device)
+                v = torch.randn(shp, generator=g, dtype=torch.float16, device=self.device)
+            self.k_pages.append(k)
+            self.v_pages.append(v)
+
+    def load_weights(self, w: dict[str, torch.Tensor]) -> None:
+        """Full (unsharded) weights -> this rank's shards on the device, registered with the
+        library.  Needs alloc_kv() first."""
+        if not self.k_pages:
+            raise RuntimeError("alloc_kv() before load_weights()")
+        s, dev = self.shape, self.device
+        self.layers = []
+        for i in range(s.n_layers):
+            full = {n: w[f"l{i}.{n}"] for n in ("attn_norm", "wqkv", "wo", "ffn_norm", "wgate", "wup", "wdown")}
+            sh = {k: v.to(dev) for k, v in tpmod.shard_layer(full, s, self.rank, self.tp).items()}
+            sh["attn_norm"] = sh["attn_norm"].float().contiguous()
+            sh["ffn_norm"] = sh["ffn_norm"].float().contiguous()
+            for k in ("wqkv", "wo", "wgate", "wup", "wdown"):
+                sh[k] = sh[k].half().contiguous()
+            self.layers.append(sh)
+            call(
+                "b2d_decoder_set_layer",
+                self._h,
+                i,
+                sh["attn_norm"].data_ptr(),
+                sh["wqkv"].data_ptr(),
+                sh["wo"].data_ptr(),
+                sh["ffn_norm"].data_ptr(),
+                sh["wgate"].data_ptr(),
+                sh["wup"].data_ptr(),
+                sh["wdown"].data_ptr(),
+                self.k_pages[i].data_ptr(),
+                self.v_pages[i].data_ptr(),
+            )
+        self.embed = w["embed"].to(dev).half().contiguous()
+        self.lm_head = tpmod.shard_head(self.embed, s, self.rank, self.tp)
+        self.final_norm = w["final_norm"].to(dev).float().contiguous()
+        call(
+            "b2d_decoder_set_head",
+            self._h,
+            self.embed.data_ptr(),
+            self.lm_head.data_ptr(),
+            self.lm_rows,
+            self.final_norm.data_ptr(),
+        )
+
+    def random_weights(self, seed: int, std: float = 0.02) -> None:
+        """Seeded random-init weights generated on the device (fp16 ~ N(0, std), norms = 1).
+        Every rank draws the same full matrices and keeps its shard."""
+        s, dev = self.shape, self.device
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+
+        def mat(m, k):
+            return (torch.randn(m, k, generator=g, device=dev, dtype=torch.float32) * std).half()
+
+        w = {"embed": mat(s.vocab, s.dim), "final_norm": torch.ones(s.dim, device=dev)}
+        for i in range(s.n_layers):
+            w[f"l{i}.attn_norm"] = torch.ones(s.dim, device=dev)
+            w[f"l{i}.wqkv"] = mat(s.qkv_dim, s.dim)
+            w[f"l{i}.wo"] = mat(s.dim, s.n_heads * s.head_dim)
+            w[f"l{i}.ffn_norm"] = torch.ones(s.dim, device=dev)
+            w[f"l{i}.wgate"] = mat(s.ffn_dim, s.dim)
+            w[f"l{i}.wup"] = mat(s.ffn_dim, s.dim)
+            w[f"l{i}.wdown"] = mat(s.dim, s.ffn_dim)
+            # shard layer by layer so the full model never sits on the device at once
+        self.load_weights(w)
+        del w
+        torch.cuda.empty_cache()
+
+    def weight_bytes(self) -> int:
+        n = sum(t.numel() * t.element_size() for L in self.layers for t in L.values())
+        return n + self.lm_head.numel() * 2 + self.final_norm.numel() * 4
+
+    # -- step -------------------------------------------------------------------------------
+
+    def step(
+        self,
+        tokens: torch.Tensor,
+        ctx_lens: torch.Tensor,
+        block_table: torch.Tensor,
+        next_tokens: torch.Tensor,
+        logits: torch.Tensor | None = None,
+        use_graph: bool = True,
+    ) -> torch.Tensor:
+        """Enqueue one decode step on self.stream (no host sync).  tokens/ctx_lens/next_tokens
+        int32 [B]; block_table int32 [B, max_blocks]; logits (optional) fp32 [B, lm_rows]."""
+        B = tokens.numel()
+        for t in (tokens, ctx_lens, block_table, next_tokens):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("tokens, ctx_lens, block_table, next_tokens: contiguous CUDA int32")
+        if block_table.shape != (B, self.max_blocks):
+            raise ValueError(f"block_table must be [{B}, {self.max_blocks}]")
+        call(
+            "b2d_decoder_step",
+            self._h,
+            tokens.data_ptr(),
+            ctx_lens.data_ptr(),
+            block_table.data_ptr(),
+            B,
+            next_tokens.data_ptr(),
+            None if logits is None else logits.data_ptr(),
+            1 if use_graph else 0,
+            self.stream.cuda_stream,
+        )
+        return next_tokens
+
+    def close(self) -> None:
+        if self._h:
+            _lib.lib().b2d_decoder_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def make_block_table(ctx_lens, max_blocks: int, n_blocks: int, seed: int, headroom: int = 1):
+    """Seeded random page assignment: sequence b gets ceil((ctx_b + headroom)/16) distinct
+    physical pages from a random permutation of [0, n_blocks).  Returns int32 [B, max_blocks]
+    (unused entries -1) on the CPU."""
+    import numpy as np
+
+    need = [-(-(int(c) + headroom) // PAGE) for c in ctx_lens]
+    if sum(need) > n_blocks:
+        raise ValueError("page pool too small")
+    perm = np.random.default_rng(seed).permutation(n_blocks)
+    table = np.full((len(need), max_blocks), -1, dtype=np.int32)
+    o = 0
+    for b, k in enumerate(need):
+        table[b, :k] = perm[o : o + k]
+        o += k
+    return torch.from_numpy(table)

@@ -1,0 +1,253 @@
+/*
+ * b200dec.h -- C ABI of the B200 (sm_100a) decode-step hot path.
+ *
+ * The reference project (ios_kernels, a Metal/Swift LLM runtime) has no in-process operator
+ * API: its decode kernels are private to the Swift Engine and bound through Metal buffer
+ * slots.  Each entry point below replaces one of those kernels or host helpers; the comment
+ * above it names the reference lines it stands in for (LK = ios_kernels/kernels/
+ * unsloth__Llama-3.2-1B-Instruct/kernel_metal_f16_20261024-1620, GK = ios_kernels/kernels/
+ * google__gemma-4-E2B-it/kernel_metal_f16_20261025-1225).
+ *
+ * Conventions
+ *  - Every pointer argument is DEVICE memory unless the comment says "host".  The caller owns
+ *    all memory; no entry point allocates, except b2d_decoder_create (explicit handle).
+ *  - Every call is stream-ordered on `stream` (a cudaStream_t; NULL = legacy default stream)
+ *    and returns an int status: 0 = B2D_OK, otherwise a B2D_ERR_* code.  Nothing aborts or
+ *    traps; b2d_status_string() names the code.  A CUDA launch error is returned as
+ *    B2D_ERR_CUDA and its cudaError_t is kept in b2d_last_cuda_error().
+ *  - Matrices are row-major [M, K] (out_features x in_features), like the reference's weights
+ *    file (LK/convert_weights.py:60-72).  Activations are [batch, K] with a row stride.
+ *  - Vector loads are 16 bytes wide: weight rows and activation rows must start on 16-byte
+ *    boundaries (B2D_ERR_ALIGN otherwise).
+ *
+ * Extension formats (no reference code exists; BASELINE config 3/4):
+ *  - Q8_32: int8 q[M, K] in [-127, 127] + fp16 scales[M, K/32];  w = float(s) * q  (exact).
+ *  - Q4_32: uint8 q[M, K/2], element 2j in the low nibble of byte j, 2j+1 in the high nibble,
+ *           nibble n -> ((n ^ 8) - 8) in [-8, 7]; fp16 scales[M, K/32].
+ *  - Paged KV cache: per layer, K and V pages of [n_blocks][Hkv][16][HD] fp16; a block table
+ *    int32[batch][max_blocks] maps token j of sequence b to page table[b][j/16], slot j%16.
+ */
+#ifndef B200DEC_H
+#define B200DEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2D_API __attribute__((visibility("default")))
+#else
+#define B2D_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* b2d_stream_t; /* same type as cudaStream_t */
+
+enum b2d_status {
+  B2D_OK = 0,
+  B2D_ERR_NULL = 1,        /* a required pointer is NULL */
+  B2D_ERR_SHAPE = 2,       /* sizes out of range or not supported by the kernel */
+  B2D_ERR_ALIGN = 3,       /* pointer or row stride not 16-byte aligned */
+  B2D_ERR_UNSUPPORTED = 4, /* dtype / epilogue / head_dim combination not built */
+  B2D_ERR_WORKSPACE = 5,   /* workspace missing or smaller than the *_workspace_bytes query */
+  B2D_ERR_CUDA = 6,        /* a CUDA runtime call failed (see b2d_last_cuda_error) */
+  B2D_ERR_NCCL = 7,        /* an NCCL call failed */
+  B2D_ERR_TIMEOUT = 8,     /* a bounded device-side wait gave up */
+  B2D_ERR_STATE = 9        /* handle used out of order (e.g. step before weights are set) */
+};
+
+enum b2d_dtype { B2D_F32 = 0, B2D_F16 = 1, B2D_Q8_32 = 2, B2D_Q4_32 = 3 };
+
+/* GEMV epilogues (GK/kernels.metal:151-198 EPI 0/1/2; LK/kernels.metal:139-173; :307-345). */
+enum b2d_epilogue {
+  B2D_EPI_STORE = 0,    /* y = W x                                */
+  B2D_EPI_ADD = 1,      /* y += W x          (residual add)       */
+  B2D_EPI_GELU_MUL = 2, /* y = gelu_tanh(W x) * aux                */
+  B2D_EPI_SWIGLU = 3,   /* y = silu(W x) * (W_up x)                */
+  B2D_EPI_ARGMAX = 4    /* logits = W x (optional), token = argmax */
+};
+
+B2D_API const char* b2d_status_string(int status);
+B2D_API int b2d_last_cuda_error(void);
+B2D_API int b2d_version(void);
+/* Kernel launches the library has enqueued from the calling thread so far (launches made
+ * while a stream is being captured into a CUDA graph count once, at capture). */
+B2D_API long long b2d_launch_counter(void);
+
+/* ---------------------------------------------------------------------------------------
+ * GEMV family (decode matrix-vector products on CUDA cores; 16-byte streaming loads)
+ * ------------------------------------------------------------------------------------- */
+
+/* Config 1: y[M] = W[M,K] x[K], all fp32, fp32 accumulation.
+ * Replaces matvec_f16 (LK/kernels.metal:106-137; host Engine.matvec LK/main.swift:248-259)
+ * for fp32 weights.  K % 4 == 0. */
+B2D_API int b2d_gemv_f32(const float* W, const float* x, float* y, int M, int K, b2d_stream_t stream);
+
+/* The fused decode GEMV.  For each of `batch` activation rows x_b (row stride ldx elements):
+ *   prologue  if gamma != NULL:  x_b <- x_b * rsqrt(mean(x_b^2) + eps) * gamma
+ *             (rmsnorm LK/kernels.metal:71-89 fused in front of the matvec, LK/main.swift:333-334)
+ *   product   acc_b = W x_b   with W of w_dtype (F32, F16, Q8_32, Q4_32; scales for Q*)
+ *   epilogue  per `epilogue` into y (row stride ldy, y_dtype F32 or F16):
+ *             STORE / ADD (matvec_f16<ADD> LK/kernels.metal:106-137),
+ *             GELU_MUL with aux[batch, M] (stride ldy) (GK/kernels.metal:159-198),
+ *             SWIGLU with the second matrix W_up/W_up_scales (matvec_gate_up_silu
+ *             LK/kernels.metal:144-173).
+ * x_dtype is F32 or F16.  K must be a multiple of 32 for Q*, 8 for F16, 4 for F32.
+ * batch >= 1 (rows are processed in groups; batch <= 8 streams W once).
+ * ARGMAX is served by b2d_lm_head_argmax. */
+B2D_API int b2d_gemv(int w_dtype, const void* W, const void* W_scales, const void* W_up,
+             const void* W_up_scales, int x_dtype, const void* x, int ldx, const float* gamma,
+             float eps, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+             int K, int batch, b2d_stream_t stream);
+
+/* Config 2 shorthand: fp16 W, fp32 x and y, fused RMSNorm (gamma may be NULL), batch rows. */
+B2D_API int b2d_rmsnorm_gemv_f16(const uint16_t* W, const float* x, const float* gamma, float eps,
+                         float* y, int M, int K, int batch, int epilogue, const float* aux,
+                         const uint16_t* W_up, b2d_stream_t stream);
+
+/* Config 3 shorthands: 32-block quantized weights, fp16 activations x[batch,K], fp32 y[batch,M]. */
+B2D_API int b2d_gemv_q8_32(const int8_t* q, const uint16_t* scales, const uint16_t* x, float* y, int M,
+                   int K, int batch, b2d_stream_t stream);
+B2D_API int b2d_gemv_q4_32(const uint8_t* q, const uint16_t* scales, const uint16_t* x, float* y, int M,
+                   int K, int batch, b2d_stream_t stream);
+
+/* Dequantize to fp32 w[M,K] = float(scale) * q, exact (bit-exact test target). */
+B2D_API int b2d_dequant_q8_32(const int8_t* q, const uint16_t* scales, float* w, int M, int K,
+                      b2d_stream_t stream);
+B2D_API int b2d_dequant_q4_32(const uint8_t* q, const uint16_t* scales, float* w, int M, int K,
+                      b2d_stream_t stream);
+
+/* LM head + greedy sampling fused: logits_b = W (rmsnorm(x_b) if gamma) with fp16 W [V, K],
+ * fp32 x; tokens[b] = argmax (ties -> lowest index) + index_offset; optional outputs
+ * logits[batch, V] (fp32, NULL to skip) and max_vals[batch] (the winning logit, NULL to skip).
+ * Replaces lmHeadAndArgmax (LK/main.swift:305-315) + argmax (LK/kernels.metal:310-345).
+ * Needs workspace of b2d_lm_head_argmax_workspace_bytes(V, batch) bytes, zero-filled before
+ * its first use; every call leaves its arrival counter at zero again for the next call. */
+B2D_API size_t b2d_lm_head_argmax_workspace_bytes(int V, int batch);
+B2D_API int b2d_lm_head_argmax(const uint16_t* W, const float* x, int ldx, const float* gamma, float eps,
+                       int V, int K, int batch, int index_offset, float* logits,
+                       int* tokens, float* max_vals, void* workspace, size_t workspace_bytes,
+                       b2d_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Small ops of the decode step
+ * ------------------------------------------------------------------------------------- */
+
+/* y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w, rows of length D, fp32 (LK/kernels.metal:71-89). */
+B2D_API int b2d_rmsnorm(const float* x, const float* w, float* y, int rows, int D, float eps,
+                b2d_stream_t stream);
+
+/* x[b, :] = float(E[tokens[b], :]), fp16 E [V, D] (embed LK/kernels.metal:31-39). */
+B2D_API int b2d_embed_f16(const uint16_t* E, const int* tokens, float* x, int D, int batch,
+                  b2d_stream_t stream);
+
+/* tokens[b] = argmax(logits[b, :N]) + index_offset, ties -> lowest (LK/kernels.metal:310-345). */
+B2D_API int b2d_argmax_f32(const float* logits, int N, int batch, int* tokens, int index_offset,
+                   b2d_stream_t stream);
+
+/* Combine per-rank (value, index) candidates [n_parts][batch] -> tokens[batch] (ties ->
+ * lowest index).  Used after the vocab-parallel LM head's all-gather. */
+B2D_API int b2d_argmax_combine(const float* vals, const int* idxs, int n_parts, int batch, int* tokens,
+                       b2d_stream_t stream);
+
+/* x[i] += p[i], fp32, n elements (residual add after a tensor-parallel all-reduce). */
+B2D_API int b2d_add_f32(float* x, const float* p, size_t n, b2d_stream_t stream);
+
+/* RoPE inverse frequencies, computed in double and rounded to fp32 (LK/main.swift:90-94);
+ * out is HOST memory of head_dim/2 floats. */
+B2D_API int b2d_inv_freq(int head_dim, double theta, float* out_host);
+
+/* ---------------------------------------------------------------------------------------
+ * Paged decode attention (ragged batch, GQA, RoPE, KV append, split-K)
+ * ------------------------------------------------------------------------------------- */
+
+/* RoPE + KV append only (rope_kv LK/kernels.metal:182-224, paged): for each sequence b with
+ * pos = ctx_lens[b], rotate q heads in place in qkv (row stride ldqkv elements, layout
+ * [q Hq*HD | k Hkv*HD | v Hkv*HD], qkv_dtype F32 or F16), rotate k and write k, v as fp16
+ * into the pages at pos (not written if the page id is outside [0, n_blocks)). */
+B2D_API int b2d_rope_kv_append(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages,
+                       uint16_t* v_pages, const int* block_table, int max_blocks,
+                       int n_blocks, const int* ctx_lens, const float* inv_freq, int n_heads, int n_kv_heads,
+                       int head_dim, int batch, b2d_stream_t stream);
+
+/* Single-query attention for each sequence b of the batch over tokens [start, pos] of its
+ * paged cache, pos = ctx_lens[b], start = max(0, pos + 1 - window) (window 0 = full).
+ * Replaces attention (LK/kernels.metal:235-305; window GK/kernels.metal:343) and, when
+ * `append` != 0, rope_kv (LK/kernels.metal:182-224): q and the new k are rotated at pos, and
+ * k, v are written into the pages at pos before use.  With append == 0 the caller has already
+ * rotated q and stored the token at pos (e.g. b2d_rope_kv_append).
+ * Split-K: keys are cut into chunks of b2d_attn_chunk_tokens(batch, n_kv_heads, max_ctx)
+ * keys; each (sequence, KV head, chunk) is one CTA whose GQA query heads share every K/V
+ * load; partial softmax states go to `workspace` and the last CTA of each (sequence, KV head)
+ * merges them.  The workspace must be zero-filled before its first use; every call leaves its
+ * arrival counters at zero again, so it can be reused by later calls on the same stream.
+ * out[b, Hq*HD] (row stride ldout, out_dtype F32 or F16).  head_dim 64, 128 or 256; n_heads /
+ * n_kv_heads in {1, 2, 4, 8}.  scale <= 0 means 1/sqrt(head_dim) (LK/main.swift:293).
+ * max_ctx bounds every ctx_lens[b] + 1 and sizes the workspace; n_blocks is the page-pool
+ * size: a block-table entry outside [0, n_blocks) is never dereferenced (its keys are
+ * skipped). */
+B2D_API int b2d_attn_chunk_tokens(int batch, int n_kv_heads, int max_ctx);
+B2D_API size_t b2d_paged_attn_workspace_bytes(int batch, int n_heads, int n_kv_heads, int head_dim,
+                                      int max_ctx);
+B2D_API int b2d_paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages,
+                          uint16_t* v_pages, const int* block_table, int max_blocks,
+                          int n_blocks, const int* ctx_lens, const float* inv_freq,
+                          int n_heads, int n_kv_heads, int head_dim, int batch, int max_ctx,
+                          float scale, int window, int append, void* out, int out_dtype,
+                          int ldout, void* workspace, size_t workspace_bytes,
+                          b2d_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Decode step of a Llama-style model (Engine.encodeDecode LK/main.swift:321-347), ragged
+ * batch over a paged cache, optionally tensor-parallel over NCCL.
+ * ------------------------------------------------------------------------------------- */
+
+typedef struct b2d_decoder b2d_decoder;
+
+typedef struct {
+  int dim, n_layers, n_heads, n_kv_heads, head_dim, ffn_dim, vocab;
+  float eps;
+  double rope_theta;
+  int max_batch;      /* largest batch a step may use */
+  int max_ctx;        /* every ctx_lens[b] + 1 <= max_ctx */
+  int max_blocks;     /* block-table row length (>= ceil(max_ctx / 16)) */
+  int n_blocks;       /* pages in each layer's K (and V) page pool */
+} b2d_model_config;
+
+/* NCCL unique id (128 bytes) for tensor parallelism; call on rank 0 and share the bytes. */
+B2D_API int b2d_nccl_unique_id_bytes(void);
+B2D_API int b2d_nccl_get_unique_id(void* out_host);
+
+/* Create a decoder for rank `tp_rank` of `tp_size` on the current CUDA device.  With
+ * tp_size > 1, nccl_id (host, 128 bytes from rank 0) sets up the communicator.  The handle
+ * allocates its activation buffers once; weights and KV pages stay owned by the caller. */
+B2D_API int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
+                       const void* nccl_id, b2d_decoder** out);
+B2D_API int b2d_decoder_destroy(b2d_decoder* h);
+
+/* Weights of this rank's shard (fp16 matrices, fp32 norms), as b2d_shard_* in the Python
+ * host lays them out: wqkv [(Hq+2Hkv)/tp*HD, D] rows [q | k | v] of the local heads;
+ * wo [D, Hq/tp*HD]; wgate, wup [F/tp, D]; wdown [D, F/tp]. */
+B2D_API int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,
+                          const uint16_t* wqkv, const uint16_t* wo, const float* ffn_norm,
+                          const uint16_t* wgate, const uint16_t* wup, const uint16_t* wdown,
+                          uint16_t* k_pages, uint16_t* v_pages);
+/* embed [V, D] fp16 (replicated); lm_head [ceil(V/tp), D] fp16 rows of this rank's vocab
+ * shard (the tied embedding's rows); final_norm [D]. */
+B2D_API int b2d_decoder_set_head(b2d_decoder* h, const uint16_t* embed, const uint16_t* lm_head,
+                         int lm_rows, const float* final_norm);
+
+/* One decode step: tokens[b] at position ctx_lens[b] for b < batch.  Writes next_tokens[b]
+ * (greedy) and, if logits != NULL, this rank's vocab-shard logits [batch, lm_rows].  The KV
+ * pages receive the new token.  use_graph != 0 captures the step into a CUDA graph on first
+ * use (per batch size and pointer set) and replays it afterwards. */
+B2D_API int b2d_decoder_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
+                     const int* block_table, int batch, int* next_tokens, float* logits,
+                     int use_graph, b2d_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200DEC_H */
