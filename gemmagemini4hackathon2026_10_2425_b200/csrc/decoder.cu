@@ -216,8 +216,11 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   }
   h->layers.resize(c.n_layers);
   const int B = c.max_batch, D = c.dim;
-  h->attn_ws_bytes =
-      paged_attn_workspace_bytes(B, h->hq, h->hk, c.head_dim, c.max_ctx);
+  // the split-K chunk size depends on the batch, so size for the worst batch of any step
+  h->attn_ws_bytes = 0;
+  for (int b = 1; b <= B; ++b)
+    h->attn_ws_bytes = std::max(h->attn_ws_bytes,
+                                paged_attn_workspace_bytes(b, h->hq, h->hk, c.head_dim, c.max_ctx));
   h->am_ws_bytes = lm_head_argmax_workspace_bytes(h->lm_rows, B);
   size_t sizes[] = {
       (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,

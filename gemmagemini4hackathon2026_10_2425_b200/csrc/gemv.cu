@@ -493,6 +493,7 @@ int gemv_dispatch(int w_dtype, const void* W, const void* W_scales, const void* 
   if (w_dtype < B2D_F32 || w_dtype > B2D_Q4_32) return B2D_ERR_UNSUPPORTED;
   const int kmul = quant ? 32 : (w_dtype == B2D_F16 ? 8 : 4);
   if (K % kmul) return B2D_ERR_SHAPE;
+  if (x_dtype == B2D_F16 && K % 8) return B2D_ERR_SHAPE;  // fp16 rows are staged 8 at a time
   if (quant && (!W_scales || (epilogue == B2D_EPI_SWIGLU && !W_up_scales)))
     return B2D_ERR_NULL;
   if (epilogue == B2D_EPI_SWIGLU && !W_up) return B2D_ERR_NULL;

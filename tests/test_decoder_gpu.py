@@ -8,7 +8,7 @@ from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, make_blo
 from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
 from oracle import ops as O
 from oracle import step as S
-from tests._tol import assert_rel_close
+from tests._tol import assert_norm_close, assert_rel_close
 from tests.test_oracle_golden import _tiny_cfg, _tiny_weights, build_paged_cache
 
 pytestmark = pytest.mark.gpu
@@ -52,8 +52,10 @@ def test_decode_step_matches_hf_golden(golden, use_graph):
     ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, [k.copy() for k in kp], [v.copy() for v in vp])
     assert_rel_close(logits, ref_logits, 2e-3, what="logits vs oracle")
     for b in range(len(lens)):
+        # HF keeps K/V in fp32, the engine (like the reference) in fp16: compare max-normalized
         hf = golden[f"llm_s{b}_logits"]
-        assert_rel_close(logits[b], hf, 2e-2, what="logits vs HF (fp16 KV cache)")
+        assert_norm_close(logits[b], hf, 1e-2, what="logits vs HF (fp16 KV cache)")
+        assert int(np.argmax(logits[b])) == int(np.argmax(hf))
     np.testing.assert_array_equal(nxt, ref_next)
 
 
@@ -69,11 +71,17 @@ def test_decode_step_llama_shape_small_batch():
     kp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
     vp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
     tokens = r.integers(0, cfg.vocab, size=len(lens)).tolist()
+    kp_orig_v = [v.copy() for v in vp]
     logits, nxt, gk, gv = run_engine(cfg, w, tokens, lens, table, kp, vp)
     ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, kp, vp)
     assert_rel_close(logits, ref_logits, 2e-3)
     srt = np.sort(ref_logits, axis=1)
     safe = (srt[:, -1] - srt[:, -2]) > 2e-3 * np.abs(srt[:, -1])
     np.testing.assert_array_equal(nxt[safe], ref_next[safe])
-    for a, b in zip(gv, vp):
-        np.testing.assert_array_equal(a.view(np.uint16), b.view(np.uint16))
+    # the appended token lands exactly in its page slot; its value comes from the fp32 QKV
+    # GEMV, so it may differ from the float64 oracle by one fp16 rounding
+    for a, b, orig in zip(gv, vp, kp_orig_v):
+        changed_gpu = np.any(a.view(np.uint16) != orig.view(np.uint16), axis=-1)
+        changed_ref = np.any(b.view(np.uint16) != orig.view(np.uint16), axis=-1)
+        np.testing.assert_array_equal(changed_gpu, changed_ref)
+        np.testing.assert_allclose(a.astype(np.float32), b.astype(np.float32), rtol=2e-3, atol=2e-3)

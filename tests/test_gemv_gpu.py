@@ -1,7 +1,8 @@
 """Parity of the GEMV family (CUDA, through the C ABI) with the float64 CPU oracle.
 
-Tolerances: 1e-5 relative for the fp32 path, 2e-3 for fp16 / quantized
-paths, elementwise with a floor of 1e-3 * max|ref|; dequantized weights bit-exact.
+Tolerances: 1e-5 relative for the fp32 path (max-normalized: fp32
+accumulation error scales with the terms, not with each result), 2e-3 for fp16 / quantized
+paths (elementwise with a floor of 1e-3 * max|ref|); dequantized weights bit-exact.
 """
 
 import numpy as np
@@ -10,7 +11,7 @@ import torch
 
 from gemmagemini4hackathon2026_10_2425_b200 import ops
 from oracle import ops as O
-from tests._tol import assert_rel_close
+from tests._tol import assert_norm_close, assert_rel_close
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -30,7 +31,7 @@ def test_gemv_f32_config1():
     W = (r.standard_normal((2048, 2048)) * 0.02).astype(np.float32)
     x = r.standard_normal(2048).astype(np.float32)
     y = ops.gemv_f32(t(W), t(x)).cpu().numpy()
-    assert_rel_close(y, O.gemv(W, x), 1e-5, what="gemv_f32")
+    assert_norm_close(y, O.gemv(W, x), 1e-5, what="gemv_f32")
 
 
 @pytest.mark.parametrize("M,K", [(2048, 4), (37, 36), (5, 4096), (3000, 2048)])
@@ -38,7 +39,7 @@ def test_gemv_f32_odd_shapes(M, K):
     r = rng(M + K)
     W = r.standard_normal((M, K)).astype(np.float32)
     x = r.standard_normal(K).astype(np.float32)
-    assert_rel_close(ops.gemv_f32(t(W), t(x)).cpu().numpy(), O.gemv(W, x), 1e-5)
+    assert_norm_close(ops.gemv_f32(t(W), t(x)).cpu().numpy(), O.gemv(W, x), 1e-5)
 
 
 def _f16_case(M, K, b, seed):
