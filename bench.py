@@ -230,7 +230,9 @@ def time_launches(fn, n_iter: int, stream) -> float:
     return e0.elapsed_time(e1) / n_iter
 
 
-def op_benchmarks(peak: float) -> dict:
+def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None) -> dict:
+    """Configs 1-4 as separate timed loops.  `only` runs the single op whose key starts with it
+    (used for ncu captures); `iters` overrides the timed iterations."""
     import torch
 
     from gemmagemini4hackathon2026_10_2425_b200 import ops
@@ -244,32 +246,43 @@ def op_benchmarks(peak: float) -> dict:
     def copies(nbytes):  # enough distinct operand copies to exceed 2x L2
         return max(1, -(-(2 * L2) // nbytes))
 
+    def want(key):  # key selected, or a prefix of the selected key (outer loops)
+        return only is None or key.startswith(only) or only.startswith(key)
+
+    def nit(default):
+        return iters if iters is not None else default
+
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     # config 1: fp32 2048x2048
     M = K = 2048
-    n = copies(M * K * 4)
-    Ws = [torch.randn(M, K, generator=g, device=dev) * 0.02 for _ in range(n)]
-    x = torch.randn(K, generator=g, device=dev)
-    y = torch.empty(M, device=dev)
-    ms = time_launches(lambda i: ops.gemv_f32(Ws[i % n], x, y), 200, s)
-    b = M * K * 4 + K * 4 + M * 4
-    res["c1_f32_2048x2048"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
-    del Ws
+    if want("c1_f32_2048x2048"):
+        n = copies(M * K * 4)
+        Ws = [torch.randn(M, K, generator=g, device=dev) * 0.02 for _ in range(n)]
+        x = torch.randn(K, generator=g, device=dev)
+        y = torch.empty(M, device=dev)
+        ms = time_launches(lambda i: ops.gemv_f32(Ws[i % n], x, y), nit(200), s)
+        b = M * K * 4 + K * 4 + M * 4
+        res["c1_f32_2048x2048"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+        del Ws
     # config 2: fp16 with fused RMSNorm
     for (K, M) in [(2048, 2048), (2048, 16384), (16384, 2048), (2048, 256000)]:
+        if not want(f"c2_f16_{K}to{M}"):
+            continue
         n = copies(M * K * 2)
         Ws = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for _ in range(n)]
         x = torch.randn(1, K, generator=g, device=dev)
         gm = 1 + 0.1 * torch.randn(K, generator=g, device=dev)
         y = torch.empty(1, M, device=dev)
-        ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), 50 if M > 100000 else 200, s)
+        ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), nit(50 if M > 100000 else 200), s)
         b = M * K * 2 + K * 4 + K * 4 + M * 4
         res[f"c2_f16_{K}to{M}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
         del Ws
     # config 3: q8 / q4, batch 1 and 16
     for fmt in ("q8", "q4"):
         for (K, M) in [(4096, 4096), (4096, 14336)]:
+            if not want(f"c3_{fmt}_{K}to{M}"):
+                continue
             wbytes = M * K * (1 if fmt == "q8" else 0.5) + M * K // 32 * 2
             n = copies(int(wbytes))
             Wq = []
@@ -281,13 +294,17 @@ def op_benchmarks(peak: float) -> dict:
                 sc = (torch.randn(M, K // 32, generator=g, device=dev) * 0.01).abs().half()
                 Wq.append(ops.QWeight(fmt, q, sc))
             for bsz in (1, 16):
+                if not want(f"c3_{fmt}_{K}to{M}_b{bsz}"):
+                    continue
                 x = torch.randn(bsz, K, generator=g, device=dev).half()
                 y = torch.empty(bsz, M, device=dev)
-                ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), 100, s)
+                ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
                 b = wbytes + bsz * K * 2 + bsz * M * 4
                 res[f"c3_{fmt}_{K}to{M}_b{bsz}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
             del Wq
     # config 4: ragged paged attention
+    if not want("c4_paged_attn_64seq"):
+        return res
     r = np.random.default_rng(4)
     B, hq, hk, hd = 64, 32, 8, 128
     lens = r.integers(128, 8193, size=B).astype(np.int32)
@@ -307,7 +324,7 @@ def op_benchmarks(peak: float) -> dict:
     invf = torch.from_numpy(O.inv_freq(hd, 10000.0)).to(dev)
     out = torch.empty(B, hq * hd, device=dev)
     ms = time_launches(
-        lambda i: ops.paged_decode_attn(qkv, kp, vp, tb, ln, invf, hq, hk, hd, max_ctx, out=out), 50, s
+        lambda i: ops.paged_decode_attn(qkv, kp, vp, tb, ln, invf, hq, hk, hd, max_ctx, out=out), nit(50), s
     )
     tot = int((lens + 1).sum())
     b = tot * hk * hd * 2 * 2 + B * (hq + 2 * hk) * hd * 2 + B * hq * hd * 4 + 4 * sum(need) + B * hk * hd * 2 * 2
@@ -506,9 +523,19 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op (configs 1-4) microbenchmarks")
+    ap.add_argument("--op", help="run only the config 1-4 microbenchmark(s) whose key starts with OP (e.g. c4, c2_f16_2048to2048) for --steps iterations, print their JSON and exit")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps
-    if args.impl == "reference":
+    if args.op:
+        import torch
+
+        from gemmagemini4hackathon2026_10_2425_b200 import _lib
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        _lib.lib()
+        peak, kind = peaks()
+        print(json.dumps({"op": args.op, "peak_gbs": peak, "peak_kind": kind, "ops": op_benchmarks(peak, only=args.op, iters=args.steps)}))
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
