@@ -73,6 +73,11 @@ SIGNATURES = {
         I,
         [P, I, I, P, P, P, I, I, P, P, I, I, I, I, I, Fl, I, I, P, I, I, P, Z, P],
     ),
+    "b2d_paged_decode_attn_noalloc_max_scratch_bytes": (Z, []),
+    "b2d_paged_decode_attn_noalloc": (
+        I,
+        [P, I, I, P, P, P, I, I, P, P, I, I, I, I, I, Fl, I, I, P, I, I, P],
+    ),
     "b2d_nccl_unique_id_bytes": (I, []),
     "b2d_nccl_get_unique_id": (I, [P]),
     "b2d_decoder_create": (I, [C.POINTER(ModelConfig), I, I, P, C.POINTER(P)]),

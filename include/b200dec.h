@@ -199,6 +199,25 @@ B2D_API int b2d_paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t*
                           int ldout, void* workspace, size_t workspace_bytes,
                           b2d_stream_t stream);
 
+/* Allocation-free variant of b2d_paged_decode_attn (no counterpart in the reference, which
+ * has no allocator constraints).  For callers that cannot allocate device memory -- code
+ * living inside another framework's memory pool, plugins whose host forbids cudaMalloc after
+ * start-up -- it takes no workspace: the split-K scratch is a fixed 16 MiB device array
+ * inside this library (held on every GPU that loads it until exit).  Sizes whose
+ * b2d_paged_attn_workspace_bytes exceed b2d_paged_decode_attn_noalloc_max_scratch_bytes()
+ * return B2D_ERR_WORKSPACE.  The first call on a device looks up the array's device address
+ * and zero-fills it synchronously, so make that first call before any stream capture.
+ * All calls share the array: calls whose kernels overlap on the GPU race on it.  Never calls
+ * cudaMalloc / cudaFree.  Other arguments and results as b2d_paged_decode_attn. */
+B2D_API size_t b2d_paged_decode_attn_noalloc_max_scratch_bytes(void);
+B2D_API int b2d_paged_decode_attn_noalloc(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages,
+                                          uint16_t* v_pages, const int* block_table,
+                                          int max_blocks, int n_blocks, const int* ctx_lens,
+                                          const float* inv_freq, int n_heads, int n_kv_heads,
+                                          int head_dim, int batch, int max_ctx, float scale,
+                                          int window, int append, void* out, int out_dtype,
+                                          int ldout, b2d_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Decode step of a Llama-style model (Engine.encodeDecode LK/main.swift:321-347), ragged
  * batch over a paged cache, optionally tensor-parallel over NCCL.
