@@ -41,6 +41,12 @@ int add_f32(float*, const float*, size_t, cudaStream_t);
 int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                    const float*, int, int, int, int, cudaStream_t);
 int attn_chunk_tokens(int, int, int);
+int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, int, int, cudaStream_t);
+int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*, int,
+                      int, cudaStream_t);
+size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
+int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
@@ -150,6 +156,28 @@ int b2d_argmax_combine(const float* vals, const int* idxs, int n_parts, int batc
 
 int b2d_add_f32(float* x, const float* p, size_t n, b2d_stream_t stream) {
   return add_f32(x, p, n, S(stream));
+}
+
+int b2d_add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps, uint16_t* out,
+                        int rows, int D, b2d_stream_t stream) {
+  return add_rmsnorm_f16(x, p, gamma, eps, out, rows, D, S(stream));
+}
+
+int b2d_embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
+                          float eps, uint16_t* out, int D, int batch, b2d_stream_t stream) {
+  return embed_rmsnorm_f16(E, tokens, x, gamma, eps, out, D, batch, S(stream));
+}
+
+size_t b2d_gemm_tc_workspace_bytes(int M, int K, int batch, int epilogue) {
+  return tc_gemm_workspace_bytes(M, K, batch, epilogue);
+}
+
+int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx, int epilogue,
+                int y_dtype, void* y, int ldy, const float* aux, int M, int K, int batch,
+                float* logits, int* tokens, float* max_vals, int index_offset, void* workspace,
+                size_t workspace_bytes, b2d_stream_t stream) {
+  return tc_gemm(W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits, tokens,
+                 max_vals, index_offset, workspace, workspace_bytes, S(stream));
 }
 
 int b2d_inv_freq(int head_dim, double theta, float* out_host) {

@@ -39,7 +39,16 @@ size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
                       void*, size_t, cudaStream_t);
+int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, int, int, cudaStream_t);
+int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*, int,
+                      int, cudaStream_t);
+size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
+int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
 }  // namespace b2d
+
+// Batches of at least this many sequences run their projections on the tensor cores.
+static constexpr int kTcMinBatch = 9;
 
 using namespace b2d;
 
@@ -92,6 +101,12 @@ struct b2d_decoder {
   size_t attn_ws_bytes = 0;
   void* am_ws = nullptr;
   size_t am_ws_bytes = 0;
+  // tensor-core path (batch >= kTcMinBatch): fp16 activation operands + GEMM workspace
+  uint16_t* xn16 = nullptr;   // [B, D]   rmsnorm(x) * gamma, fp16
+  uint16_t* att16 = nullptr;  // [B, hq*HD]
+  uint16_t* h16 = nullptr;    // [B, fl]
+  void* tc_ws = nullptr;
+  size_t tc_ws_bytes = 0;
   // graph cache
   cudaGraphExec_t gexec = nullptr;
   GraphKey gkey;
@@ -107,10 +122,80 @@ static int cuda_status(cudaError_t e) {
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
+// Tensor-core step (batch >= kTcMinBatch): activations enter each projection as fp16
+// (RMSNorm fused into the producer of the operand), weights are read once per step.
+static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_lens,
+                           const int* block_table, int B, int* next_tokens, float* logits,
+                           cudaStream_t s) {
+  const b2d_model_config& c = h->cfg;
+  const int D = c.dim, HD = c.head_dim, HQD = h->hq * c.head_dim;
+  const bool tpar = h->tp > 1;
+  void* ws = h->tc_ws;
+  const size_t wsb = h->tc_ws_bytes;
+  B2D_TRY(embed_rmsnorm_f16(h->embed, tokens, h->x, h->layers[0].attn_norm, c.eps, h->xn16, D, B,
+                            s));
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Layer& L = h->layers[l];
+    const float* next_norm = l + 1 < c.n_layers ? h->layers[l + 1].attn_norm : h->final_norm;
+    // QKV (column-parallel)
+    B2D_TRY(tc_gemm(L.wqkv, nullptr, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
+                    nullptr, h->qkv_l, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+    // RoPE + KV append + split-K attention -> fp16 operand of the O projection
+    B2D_TRY(paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
+                              c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
+                              c.max_ctx, 0.f, 0, 1, h->att16, B2D_F16, HQD, h->attn_ws,
+                              h->attn_ws_bytes, s));
+    // O projection (row-parallel) + residual, then RMSNorm(ffn) -> fp16
+    if (!tpar) {
+      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
+                      HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, B, D, s));
+    } else {
+      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_STORE, B2D_F32, h->part, D, nullptr,
+                      D, HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+      B2D_TRY(nccl_status(
+          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
+      B2D_TRY(add_rmsnorm_f16(h->x, h->part, L.ffn_norm, c.eps, h->xn16, B, D, s));
+    }
+    // gate/up SwiGLU (column-parallel) -> fp16
+    B2D_TRY(tc_gemm(L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, B2D_F16, h->h16, h->fl, nullptr,
+                    h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+    // down (row-parallel) + residual, then the next RMSNorm -> fp16
+    if (!tpar) {
+      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
+                      h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, B, D, s));
+    } else {
+      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_STORE, B2D_F32, h->part, D,
+                      nullptr, D, h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+      B2D_TRY(nccl_status(
+          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
+      B2D_TRY(add_rmsnorm_f16(h->x, h->part, next_norm, c.eps, h->xn16, B, D, s));
+    }
+  }
+  // LM head (vocab-parallel) + argmax
+  const int offset = h->rank * h->lm_stride;
+  if (!tpar) {
+    B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
+                    h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s));
+  } else {
+    B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
+                    h->lm_rows, D, B, logits, h->my_idx, h->my_val, offset, ws, wsb, s));
+    B2D_TRY(nccl_status(ncclGroupStart()));
+    B2D_TRY(nccl_status(ncclAllGather(h->my_val, h->cand_val, B, ncclFloat, h->comm, s)));
+    B2D_TRY(nccl_status(ncclAllGather(h->my_idx, h->cand_idx, B, ncclInt32, h->comm, s)));
+    B2D_TRY(nccl_status(ncclGroupEnd()));
+    B2D_TRY(argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s));
+  }
+  return B2D_OK;
+}
+
 // Enqueue one decode step on `s` (no synchronization, graph-capturable).
 static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                         const int* block_table, int B, int* next_tokens, float* logits,
                         cudaStream_t s) {
+  if (B >= kTcMinBatch)
+    return enqueue_step_tc(h, tokens, ctx_lens, block_table, B, next_tokens, logits, s);
   const b2d_model_config& c = h->cfg;
   const int D = c.dim, HD = c.head_dim;
   const bool tpar = h->tp > 1;
@@ -222,11 +307,26 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
     h->attn_ws_bytes = std::max(h->attn_ws_bytes,
                                 paged_attn_workspace_bytes(b, h->hq, h->hk, c.head_dim, c.max_ctx));
   h->am_ws_bytes = lm_head_argmax_workspace_bytes(h->lm_rows, B);
+  // tensor-core GEMM workspace: the largest of the step's call sites, for both N tiles
+  h->tc_ws_bytes = 0;
+  if (B >= kTcMinBatch) {
+    const int HQD = h->hq * c.head_dim;
+    const int shapes[5][3] = {{h->qkv_l, D, B2D_EPI_STORE},
+                              {D, HQD, B2D_EPI_ADD},
+                              {h->fl, D, B2D_EPI_SWIGLU},
+                              {D, h->fl, B2D_EPI_ADD},
+                              {h->lm_rows, D, B2D_EPI_ARGMAX}};
+    for (int b : {std::min(B, 16), B})
+      for (auto& sh : shapes)
+        h->tc_ws_bytes = std::max(h->tc_ws_bytes, tc_gemm_workspace_bytes(sh[0], sh[1], b, sh[2]));
+  }
   size_t sizes[] = {
       (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,
       (size_t)B * h->fl * 4,      (size_t)B * D * 4,        (size_t)c.head_dim / 2 * 4,
       (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)B * 4,
-      (size_t)B * 4,              h->attn_ws_bytes,         h->am_ws_bytes};
+      (size_t)B * 4,              h->attn_ws_bytes,         h->am_ws_bytes,
+      (size_t)B * D * 2,          (size_t)B * h->hq * c.head_dim * 2, (size_t)B * h->fl * 2,
+      h->tc_ws_bytes};
   size_t total = 0;
   for (size_t s : sizes) total += align256(s);
   int st = cuda_status(cudaMalloc(&h->arena, total));
@@ -239,8 +339,12 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   void** slots[] = {(void**)&h->x,        (void**)&h->qkv,      (void**)&h->att,
                     (void**)&h->hid,      (void**)&h->part,     (void**)&h->invf,
                     (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->my_val,
-                    (void**)&h->my_idx,   (void**)&h->attn_ws,  (void**)&h->am_ws};
-  for (int i = 0; i < 12; ++i) {
+                    (void**)&h->my_idx,   (void**)&h->attn_ws,  (void**)&h->am_ws,
+                    (void**)&h->xn16,     (void**)&h->att16,    (void**)&h->h16,
+                    (void**)&h->tc_ws};
+  static_assert(sizeof(slots) / sizeof(slots[0]) == sizeof(sizes) / sizeof(sizes[0]),
+                "one slot per buffer size");
+  for (size_t i = 0; i < sizeof(sizes) / sizeof(sizes[0]); ++i) {
     *slots[i] = p;
     p += align256(sizes[i]);
   }

@@ -144,4 +144,79 @@ int add_f32(float* x, const float* p, size_t n, cudaStream_t stream) {
   return launch_status();
 }
 
+// Residual add + RMSNorm to fp16 (the tensor-core GEMMs' activation operand), one CTA per row:
+//   if p: x += p (written back);   out = fp16(x * rsqrt(mean(x^2) + eps) * gamma)
+// (rmsnorm LK/kernels.metal:71-89; the add is the residual update after a tensor-parallel
+// all-reduce).  Launched with programmatic dependent launch.
+__global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const float* p,
+                                                              const float* gamma, float eps,
+                                                              uint16_t* out, int D) {
+  __shared__ float red[8];
+  pdl_wait();
+  float* xr = x + (size_t)blockIdx.x * D;
+  const float* pr = p ? p + (size_t)blockIdx.x * D : nullptr;
+  uint16_t* orow = out + (size_t)blockIdx.x * D;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += 256) {
+    float v = xr[i];
+    if (pr) {
+      v += pr[i];
+      xr[i] = v;
+    }
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float scale = rsqrtf(tot / (float)D + eps);
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < D; i += 256) orow[i] = f2h(xr[i] * scale * gamma[i]);
+}
+
+int add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps, uint16_t* out,
+                    int rows, int D, cudaStream_t stream) {
+  if (!x || !gamma || !out) return B2D_ERR_NULL;
+  if (rows <= 0 || D <= 0) return B2D_ERR_SHAPE;
+  return launch_pdl(add_rmsnorm_f16_kernel, dim3(rows), dim3(256), 0, stream, x, p, gamma, eps,
+                    out, D);
+}
+
+// Embedding gather + RMSNorm to fp16: x[b] = float(E[tokens[b]]); out[b] = fp16(norm(x[b])*gamma)
+// (embed LK/kernels.metal:31-39 fused with the first layer's rmsnorm).
+__global__ void __launch_bounds__(256) embed_rmsnorm_f16_kernel(const uint16_t* E,
+                                                                const int* tokens, float* x,
+                                                                const float* gamma, float eps,
+                                                                uint16_t* out, int D) {
+  __shared__ float red[8];
+  pdl_wait();
+  const size_t tok = (size_t)tokens[blockIdx.x];
+  const uint16_t* er = E + tok * D;
+  float* xr = x + (size_t)blockIdx.x * D;
+  uint16_t* orow = out + (size_t)blockIdx.x * D;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < D; i += 256) {
+    const float v = h2f(er[i]);
+    xr[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float scale = rsqrtf(tot / (float)D + eps);
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < D; i += 256) orow[i] = f2h(xr[i] * scale * gamma[i]);
+}
+
+int embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
+                      float eps, uint16_t* out, int D, int batch, cudaStream_t stream) {
+  if (!E || !tokens || !x || !gamma || !out) return B2D_ERR_NULL;
+  if (D <= 0 || batch <= 0) return B2D_ERR_SHAPE;
+  return launch_pdl(embed_rmsnorm_f16_kernel, dim3(batch), dim3(256), 0, stream, E, tokens, x,
+                    gamma, eps, out, D);
+}
+
 }  // namespace b2d

@@ -1,0 +1,626 @@
+// Batched decode GEMM on the 5th-generation tensor cores (sm_100a tcgen05 + TMEM + TMA).
+//
+//   Y[b, m] = epilogue( sum_k W[m, k] * X[b, k] ),  b < batch <= 32,  W fp16 [M, K], X fp16 [batch, K]
+//
+// Why tensor cores here: at batch 16-32 a decode GEMV does 32-64 flops per weight byte; keeping
+// up with ~6.5 TB/s of HBM needs 200-400 TFLOP/s, beyond the CUDA cores' fp32 FMA rate.  The
+// reference runs these projections as matvec_f16 / matvec_gate_up_silu (LK/kernels.metal:106-173)
+// once per sequence; this kernel serves the whole ragged batch in one pass over the weights.
+//
+// Structure ("swap AB": weights are the MMA's M side, tokens its N side):
+//  * one CTA per (128-row tile of W, K split); 128 threads;
+//  * warp 0 / lane 0 streams W tiles [128 x 64] (and W_up tiles for SwiGLU) and X tiles [N x 64]
+//    with TMA (cp.async.bulk.tensor, 128-byte swizzle) through a STAGES-deep shared-memory ring
+//    guarded by mbarriers.  Weight tiles do not depend on the previous kernel, so the first ring
+//    of them is issued before griddepcontrol.wait (programmatic dependent launch);
+//  * warp 1 / lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=16|32, K=16, fp32
+//    accumulate) into TMEM and frees each ring slot with tcgen05.commit;
+//  * all four warps read the accumulator tile back with tcgen05.ld (warp w owns TMEM lanes
+//    32w..32w+31 = W rows), then either finish the epilogue directly (one K split) or write fp32
+//    partials; the last CTA of each row tile (arrival counter) sums the splits in a fixed order
+//    (deterministic) and runs the epilogue: store / residual add / SwiGLU / argmax.
+//  * every mbarrier wait is bounded by a clock64 budget; on timeout the CTA records an error
+//    word in the workspace, skips the rest and still releases its TMEM.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace b2d {
+
+namespace tc {
+
+constexpr int BM = 128;        // W rows per tile (MMA M)
+constexpr int BK = 64;         // K elements per stage (128 bytes of fp16 = one swizzle row)
+constexpr int THREADS = 128;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz: bounded waits
+
+enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_DONE = 3 };
+
+struct Params {
+  CUtensorMap tmA;   // W      [M, K] fp16, box {64, 128}, 128B swizzle
+  CUtensorMap tmA2;  // W_up   (SwiGLU only)
+  CUtensorMap tmB;   // X      [batch, K] fp16, box {64, N}, 128B swizzle
+  int M, K, batch;
+  int k_tiles, k_splits, m_tiles;
+  int epi;           // B2D_EPI_*
+  void* y;
+  int y_f16;
+  int ldy;
+  const float* aux;
+  float* partials;           // [m_tiles][k_splits][nacc][BM][N]
+  unsigned int* counters;    // [m_tiles]
+  int* err;                  // error word
+  // argmax
+  float* logits;             // optional [batch][M] (ld = ldy)
+  int* tokens;
+  float* max_vals;
+  int index_offset;
+  float* am_val;             // [m_tiles][N]
+  int* am_idx;
+  unsigned int* am_counter;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and the error word set) if the phase did not complete in time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* err, int code) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, phase)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart (SBO), LBO = 1
+// (unused for swizzled K-major), descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: D fp32, A/B fp16, both K-major, M = 128, N.
+template <int N>
+__device__ __forceinline__ uint32_t idesc_f16() {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 lanes x N columns of fp32 from TMEM: thread = lane, N registers = N columns.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v);
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) {
+  tmem_ld<16>(taddr, v);
+  tmem_ld<16>(taddr + 16, v + 16);
+}
+
+template <int N, bool DUAL>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+  static constexpr int B_BYTES = N * BK * 2;           // 2 / 4 KB
+  static constexpr int STAGE_BYTES = A_BYTES * (DUAL ? 2 : 1) + B_BYTES;
+  static constexpr int STAGES = DUAL ? 5 : 8;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  static constexpr int NACC = DUAL ? 2 : 1;
+  static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
+};
+
+template <int N, bool DUAL, bool ARGMAX>
+__global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<N, DUAL>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ bool is_last;
+  __shared__ float am_v[4][N];
+  __shared__ int am_i[4][N];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m_tile = blockIdx.x, split = blockIdx.y;
+  const int m0 = m_tile * BM;
+  const int kt_begin = (int)((long long)split * p.k_tiles / p.k_splits);
+  const int kt_end = (int)((long long)(split + 1) * p.k_tiles / p.k_splits);
+  const int nkt = kt_end - kt_begin;
+
+  if (tid == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    abort_flag = 0;
+    tma_prefetch_desc(&p.tmA);
+    if (DUAL) tma_prefetch_desc(&p.tmA2);
+    tma_prefetch_desc(&p.tmB);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    const uint32_t tx = C::STAGE_BYTES;
+    const int first = min(nkt, C::STAGES);
+    for (int i = 0; i < first; ++i) {  // weight tiles: independent of the previous kernel
+      uint8_t* st = smem + i * C::STAGE_BYTES;
+      mbar_expect_tx(&full_bar[i], tx);
+      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
+      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
+    }
+    pdl_wait();  // activations come from the previous kernel
+    for (int i = 0; i < first; ++i) {
+      uint8_t* st = smem + i * C::STAGE_BYTES;
+      tma_load_2d(st + C::A_BYTES * C::NACC, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[i]);
+    }
+    for (int i = first; i < nkt; ++i) {
+      const int s = i % C::STAGES;
+      if (!mbar_wait(&empty_bar[s], ((i / C::STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+        abort_flag = 1;
+        break;
+      }
+      uint8_t* st = smem + s * C::STAGE_BYTES;
+      mbar_expect_tx(&full_bar[s], tx);
+      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[s]);
+      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[s]);
+      tma_load_2d(st + C::A_BYTES * C::NACC, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = idesc_f16<N>();
+    bool ok = true;
+    for (int i = 0; i < nkt; ++i) {
+      const int s = i % C::STAGES;
+      if (!mbar_wait(&full_bar[s], (i / C::STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint8_t* st = smem + s * C::STAGE_BYTES;
+      const uint64_t a = smem_desc_sw128(st);
+      const uint64_t b = smem_desc_sw128(st + C::A_BYTES * C::NACC);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {  // 32 bytes of K per MMA: +2 in the 16-byte address field
+        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+        mma_f16(tmem, a + 2 * k, b + 2 * k, idesc, acc);
+        if (DUAL) {
+          const uint64_t a2 = smem_desc_sw128(st + C::A_BYTES);
+          mma_f16(tmem + N, a2 + 2 * k, b + 2 * k, idesc, acc);
+        }
+      }
+      mma_commit(&empty_bar[s]);  // slot is free once these MMAs have read it
+    }
+    if (ok) mma_commit(&done_bar);
+    else abort_flag = 1;
+  }
+  __syncwarp();
+
+  // ---------------- epilogue (all 4 warps) ----------------
+  // CTA-uniform: tcgen05.ld below is warp-collective
+  const bool have =
+      __syncthreads_and(mbar_wait(&done_bar, 0, p.err, ERR_TIMEOUT_DONE) ? 1 : 0) != 0 && nkt > 0;
+  tc_fence_after();
+  float acc[N], acc2[DUAL ? N : 1];
+  if (have) {
+    const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
+    tmem_ld<N>(taddr, acc);
+    if (DUAL) tmem_ld<N>(taddr + N, acc2);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(C::TMEM_COLS));
+  }
+  if (!have || abort_flag) return;
+  pdl_wait();  // epilogue reads / writes buffers the previous kernel may touch
+  pdl_launch_dependents();
+
+  const int r = warp * 32 + lane;  // row within the tile
+  const int row = m0 + r;
+
+  if (p.k_splits > 1) {
+    float* mine = p.partials + (((size_t)m_tile * p.k_splits + split) * C::NACC) * BM * N;
+#pragma unroll
+    for (int t = 0; t < N; t += 4) {
+      *reinterpret_cast<float4*>(mine + (size_t)r * N + t) =
+          make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+      if (DUAL)
+        *reinterpret_cast<float4*>(mine + (size_t)BM * N + (size_t)r * N + t) =
+            make_float4(acc2[t], acc2[t + 1], acc2[t + 2], acc2[t + 3]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(p.counters + m_tile, 1u) == (unsigned)(p.k_splits - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+#pragma unroll
+    for (int t = 0; t < N; ++t) {
+      acc[t] = 0.f;
+      if (DUAL) acc2[t] = 0.f;
+    }
+    for (int sp = 0; sp < p.k_splits; ++sp) {  // fixed order: deterministic sums
+      const float* src = p.partials + (((size_t)m_tile * p.k_splits + sp) * C::NACC) * BM * N;
+#pragma unroll
+      for (int t = 0; t < N; t += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (size_t)r * N + t));
+        acc[t] += v.x;
+        acc[t + 1] += v.y;
+        acc[t + 2] += v.z;
+        acc[t + 3] += v.w;
+        if (DUAL) {
+          const float4 u =
+              __ldcg(reinterpret_cast<const float4*>(src + (size_t)BM * N + (size_t)r * N + t));
+          acc2[t] += u.x;
+          acc2[t + 1] += u.y;
+          acc2[t + 2] += u.z;
+          acc2[t + 3] += u.w;
+        }
+      }
+    }
+    if (tid == 0) p.counters[m_tile] = 0u;  // ready for the next launch
+  }
+
+  if constexpr (ARGMAX) {
+    // logits (optional), then per-token (max, row) over this tile
+#pragma unroll
+    for (int t = 0; t < N; ++t) {
+      float v = (row < p.M && t < p.batch) ? acc[t] : -INFINITY;
+      int idx = row < p.M ? row : 0x7fffffff;
+      if (p.logits && row < p.M && t < p.batch) p.logits[(size_t)t * p.ldy + row] = acc[t];
+      warp_argmax(v, idx);
+      if (lane == 0) {
+        am_v[warp][t] = v;
+        am_i[warp][t] = idx;
+      }
+    }
+    __syncthreads();
+    if (tid < N) {
+      float bv = am_v[0][tid];
+      int bi = am_i[0][tid];
+      for (int w = 1; w < 4; ++w)
+        if (better(am_v[w][tid], am_i[w][tid], bv, bi)) {
+          bv = am_v[w][tid];
+          bi = am_i[w][tid];
+        }
+      p.am_val[(size_t)m_tile * N + tid] = bv;
+      p.am_idx[(size_t)m_tile * N + tid] = bi;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(p.am_counter, 1u) == (unsigned)(gridDim.x * gridDim.y - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int t = warp; t < p.batch; t += 4) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int mt = lane; mt < p.m_tiles; mt += 32) {
+        const float v = __ldcg(p.am_val + (size_t)mt * N + t);
+        const int i = __ldcg(p.am_idx + (size_t)mt * N + t);
+        if (better(v, i, bv, bi)) {
+          bv = v;
+          bi = i;
+        }
+      }
+      warp_argmax(bv, bi);
+      if (lane == 0) {
+        p.tokens[t] = bi + p.index_offset;
+        if (p.max_vals) p.max_vals[t] = bv;
+      }
+    }
+    if (tid == 0) *p.am_counter = 0u;
+  } else {
+    if (row >= p.M) return;
+#pragma unroll
+    for (int t = 0; t < N; ++t) {
+      if (t >= p.batch) break;
+      const size_t yi = (size_t)t * p.ldy + row;
+      float v;
+      if (DUAL) {
+        v = silu(acc[t]) * acc2[t];
+      } else {
+        v = acc[t];
+        if (p.epi == B2D_EPI_ADD)
+          v += p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
+                       : reinterpret_cast<const float*>(p.y)[yi];
+        else if (p.epi == B2D_EPI_GELU_MUL)
+          v = gelu_tanh(v) * p.aux[yi];
+      }
+      if (p.y_f16)
+        reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(v);
+      else
+        reinterpret_cast<float*>(p.y)[yi] = v;
+    }
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------------------------------
+// host
+// ------------------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D fp16 tensor [rows, cols] with row stride ld (elements), box {64, box_rows}, 128B swizzle.
+static int make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return B2D_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2D_OK : B2D_ERR_ALIGN;
+}
+
+struct TcPlan {
+  int n_tile, m_tiles, k_tiles, k_splits, nacc;
+  size_t off_counters, off_partials, off_amv, off_ami, total;
+};
+
+static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
+  TcPlan pl{};
+  pl.n_tile = batch <= 16 ? 16 : 32;
+  pl.m_tiles = (M + tc::BM - 1) / tc::BM;
+  pl.k_tiles = (K + tc::BK - 1) / tc::BK;
+  pl.nacc = epilogue == B2D_EPI_SWIGLU ? 2 : 1;
+  if (epilogue == B2D_EPI_ARGMAX) {
+    pl.k_splits = 1;
+  } else {
+    pl.k_splits = std::max(1, std::min(num_sms() / pl.m_tiles, std::min(pl.k_tiles, 16)));
+  }
+  auto a256 = [](size_t n) { return (n + 255) / 256 * 256; };
+  size_t o = 256;  // [0]: error word, [64]: argmax arrival counter
+  pl.off_counters = o;
+  o += a256((size_t)pl.m_tiles * 4);
+  pl.off_partials = o;
+  if (pl.k_splits > 1) o += a256((size_t)pl.m_tiles * pl.k_splits * pl.nacc * tc::BM * pl.n_tile * 4);
+  pl.off_amv = o;
+  pl.off_ami = o;
+  if (epilogue == B2D_EPI_ARGMAX) {
+    o += a256((size_t)pl.m_tiles * pl.n_tile * 4);
+    pl.off_ami = o;
+    o += a256((size_t)pl.m_tiles * pl.n_tile * 4);
+  }
+  pl.total = o;
+  return pl;
+}
+
+size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue) {
+  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32) return 0;
+  return tc_plan(M, K, batch, epilogue).total;
+}
+
+template <int N, bool DUAL, bool ARGMAX>
+static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
+  using C = tc::Cfg<N, DUAL>;
+  auto kern = tc::tc_gemm_kernel<N, DUAL, ARGMAX>;
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) {
+      set_cuda_error(e);
+      return B2D_ERR_CUDA;
+    }
+    configured_dev = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(tc::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return B2D_ERR_CUDA;
+  }
+  count_launch();
+  return B2D_OK;
+}
+
+// A prepared call: tensor maps encoded once, reusable (and graph-capturable) while the
+// pointers stay the same.
+struct TcCall {
+  tc::Params prm;
+  dim3 grid;
+  int n_tile;
+  bool dual, argmax;
+};
+
+int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
+                    int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+                    int K, int batch, float* logits, int* tokens, float* max_vals,
+                    int index_offset, void* workspace, size_t workspace_bytes) {
+  if (!call || !W || !X) return B2D_ERR_NULL;
+  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8)
+    return B2D_ERR_SHAPE;
+  if (epilogue < B2D_EPI_STORE || epilogue > B2D_EPI_ARGMAX) return B2D_ERR_UNSUPPORTED;
+  if (y_dtype != B2D_F32 && y_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
+  if (epilogue == B2D_EPI_SWIGLU && !W_up) return B2D_ERR_NULL;
+  if (epilogue == B2D_EPI_GELU_MUL && !aux) return B2D_ERR_NULL;
+  if (epilogue == B2D_EPI_ARGMAX && !tokens) return B2D_ERR_NULL;
+  if (epilogue != B2D_EPI_ARGMAX && !y) return B2D_ERR_NULL;
+  if (epilogue != B2D_EPI_ARGMAX && ldy < M) return B2D_ERR_SHAPE;
+  if (!aligned16(W) || !aligned16(X) || (W_up && !aligned16(W_up))) return B2D_ERR_ALIGN;
+  const TcPlan pl = tc_plan(M, K, batch, epilogue);
+  if (!workspace || workspace_bytes < pl.total) return B2D_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return B2D_ERR_ALIGN;
+  tc::Params& p = call->prm;
+  p = tc::Params{};
+  B2D_TRY(make_map(&p.tmA, W, M, K, K, tc::BM));
+  if (W_up) B2D_TRY(make_map(&p.tmA2, W_up, M, K, K, tc::BM));
+  B2D_TRY(make_map(&p.tmB, X, batch, K, ldx, pl.n_tile));
+  char* ws = static_cast<char*>(workspace);
+  p.M = M;
+  p.K = K;
+  p.batch = batch;
+  p.k_tiles = pl.k_tiles;
+  p.k_splits = pl.k_splits;
+  p.m_tiles = pl.m_tiles;
+  p.epi = epilogue;
+  p.y = y;
+  p.y_f16 = y_dtype == B2D_F16;
+  p.ldy = epilogue == B2D_EPI_ARGMAX ? M : ldy;
+  p.aux = aux;
+  p.err = reinterpret_cast<int*>(ws);
+  p.am_counter = reinterpret_cast<unsigned int*>(ws + 64);
+  p.counters = reinterpret_cast<unsigned int*>(ws + pl.off_counters);
+  p.partials = reinterpret_cast<float*>(ws + pl.off_partials);
+  p.logits = logits;
+  p.tokens = tokens;
+  p.max_vals = max_vals;
+  p.index_offset = index_offset;
+  p.am_val = reinterpret_cast<float*>(ws + pl.off_amv);
+  p.am_idx = reinterpret_cast<int*>(ws + pl.off_ami);
+  call->grid = dim3(pl.m_tiles, pl.k_splits);
+  call->n_tile = pl.n_tile;
+  call->dual = epilogue == B2D_EPI_SWIGLU;
+  call->argmax = epilogue == B2D_EPI_ARGMAX;
+  return B2D_OK;
+}
+
+int tc_gemm_launch(const TcCall& c, cudaStream_t stream) {
+  if (c.n_tile == 16) {
+    if (c.argmax) return launch_tc<16, false, true>(c.prm, c.grid, stream);
+    if (c.dual) return launch_tc<16, true, false>(c.prm, c.grid, stream);
+    return launch_tc<16, false, false>(c.prm, c.grid, stream);
+  }
+  if (c.argmax) return launch_tc<32, false, true>(c.prm, c.grid, stream);
+  if (c.dual) return launch_tc<32, true, false>(c.prm, c.grid, stream);
+  return launch_tc<32, false, false>(c.prm, c.grid, stream);
+}
+
+int tc_gemm(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx, int epilogue,
+            int y_dtype, void* y, int ldy, const float* aux, int M, int K, int batch,
+            float* logits, int* tokens, float* max_vals, int index_offset, void* workspace,
+            size_t workspace_bytes, cudaStream_t stream) {
+  TcCall c;
+  B2D_TRY(tc_gemm_prepare(&c, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
+                          logits, tokens, max_vals, index_offset, workspace, workspace_bytes));
+  return tc_gemm_launch(c, stream);
+}
+
+}  // namespace b2d

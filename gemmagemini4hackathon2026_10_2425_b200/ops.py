@@ -342,3 +342,80 @@ def paged_decode_attn(
         _stream(),
     )
     return out
+
+
+_WS_TC = Workspace()
+_TC_EPI = {"store": _lib.EPI_STORE, "add": _lib.EPI_ADD, "gelu_mul": _lib.EPI_GELU_MUL, "swiglu": _lib.EPI_SWIGLU, "argmax": _lib.EPI_ARGMAX}
+
+
+def tc_workspace_bytes(M: int, K: int, batch: int, epilogue: str = "store") -> int:
+    return int(_lib.lib().b2d_gemm_tc_workspace_bytes(M, K, batch, _TC_EPI[epilogue]))
+
+
+def gemm_tc(
+    W: torch.Tensor,
+    X: torch.Tensor,
+    *,
+    epilogue: str = "store",
+    W_up: torch.Tensor | None = None,
+    aux: torch.Tensor | None = None,
+    y: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.float32,
+    index_offset: int = 0,
+    return_logits: bool = False,
+    workspace: torch.Tensor | None = None,
+):
+    """Tensor-core batched GEMV (tcgen05): y[b] = epilogue(W @ X[b]) for fp16 W [M, K] and fp16
+    X [batch <= 32, K].  For 'argmax' returns tokens (and logits if asked)."""
+    M, K = W.shape
+    B = X.shape[0]
+    if W.dtype != torch.float16 or X.dtype != torch.float16 or X.shape[1] != K:
+        raise ValueError("gemm_tc needs fp16 W [M, K] and fp16 X [batch, K]")
+    ws = workspace if workspace is not None else _WS_TC.get(tc_workspace_bytes(M, K, B, epilogue), X.device)
+    tokens = logits = None
+    if epilogue == "argmax":
+        tokens = torch.empty(B, dtype=torch.int32, device=X.device)
+        logits = torch.empty(B, M, dtype=torch.float32, device=X.device) if return_logits else None
+        ydt = _lib.F32
+    else:
+        if y is None:
+            if epilogue == "add":
+                raise ValueError("epilogue 'add' needs y")
+            y = torch.empty(B, M, dtype=out_dtype, device=X.device)
+        if y.dtype not in _DT or tuple(y.shape) != (B, M):
+            raise ValueError(f"y must be fp32/fp16 [{B}, {M}]")
+        ydt = _DT[y.dtype]
+    _need_cuda(W, X, W_up, aux, y, ws, tokens, logits)
+    call(
+        "b2d_gemm_tc",
+        W.data_ptr(),
+        _ptr(W_up),
+        X.data_ptr(),
+        K,
+        _TC_EPI[epilogue],
+        ydt,
+        _ptr(y),
+        M,
+        _ptr(aux),
+        M,
+        K,
+        B,
+        _ptr(logits),
+        _ptr(tokens),
+        None,
+        int(index_offset),
+        ws.data_ptr(),
+        ws.numel(),
+        _stream(),
+    )
+    if epilogue == "argmax":
+        return (tokens, logits) if return_logits else tokens
+    return y
+
+
+def add_rmsnorm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float, p: torch.Tensor | None = None) -> torch.Tensor:
+    """x += p (if given, in place); returns fp16 rmsnorm(x) * gamma."""
+    out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    _need_cuda(x, gamma, p)
+    call("b2d_add_rmsnorm_f16", x.data_ptr(), _ptr(p), gamma.data_ptr(), float(eps), out.data_ptr(), x.shape[0], x.shape[1], _stream())
+    return out

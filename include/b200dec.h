@@ -131,6 +131,23 @@ B2D_API int b2d_lm_head_argmax(const uint16_t* W, const float* x, int ldx, const
                        int* tokens, float* max_vals, void* workspace, size_t workspace_bytes,
                        b2d_stream_t stream);
 
+/* Batched decode GEMM on the tensor cores (tcgen05.mma with TMEM accumulators, operands staged
+ * by TMA) for 1 <= batch <= 32 -- the batch >= 16 path of matvec_f16 / matvec_gate_up_silu
+ * (LK/kernels.metal:106-173) and lmHeadAndArgmax (LK/main.swift:305-315):
+ *   Y[b, m] = epilogue(sum_k W[m, k] X[b, k]),  W fp16 [M, K] row-major, X fp16 [batch, K]
+ *   (row stride ldx, a multiple of 8), K a multiple of 8.
+ * Epilogues: STORE / ADD (y fp32 or fp16, row stride ldy), GELU_MUL (aux), SWIGLU (W_up: both
+ * matrices share each X tile), ARGMAX (tokens[b] = argmax + index_offset, ties -> lowest index;
+ * logits[batch, M] and max_vals[batch] optional, y unused).  Split-K partial sums are reduced
+ * in a fixed order (deterministic).  Workspace: b2d_gemm_tc_workspace_bytes(M, K, batch,
+ * epilogue) bytes, zero-filled before first use; its first int is an error word (non-zero after
+ * a bounded device-side wait gave up); calls leave its counters at zero. */
+B2D_API size_t b2d_gemm_tc_workspace_bytes(int M, int K, int batch, int epilogue);
+B2D_API int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
+                        int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
+                        int batch, float* logits, int* tokens, float* max_vals, int index_offset,
+                        void* workspace, size_t workspace_bytes, b2d_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Small ops of the decode step
  * ------------------------------------------------------------------------------------- */
@@ -151,6 +168,18 @@ B2D_API int b2d_argmax_f32(const float* logits, int N, int batch, int* tokens, i
  * lowest index).  Used after the vocab-parallel LM head's all-gather. */
 B2D_API int b2d_argmax_combine(const float* vals, const int* idxs, int n_parts, int batch, int* tokens,
                        b2d_stream_t stream);
+
+/* Residual add + RMSNorm to fp16 (the tensor-core GEMM operand), rows of length D:
+ * if p != NULL: x += p (x updated in place); out = fp16(x * rsqrt(mean(x^2) + eps) * gamma).
+ * (rmsnorm LK/kernels.metal:71-89.) */
+B2D_API int b2d_add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps,
+                                uint16_t* out, int rows, int D, b2d_stream_t stream);
+
+/* Embedding + RMSNorm: x[b] = float(E[tokens[b]]); out[b] = fp16(rmsnorm(x[b]) * gamma)
+ * (embed LK/kernels.metal:31-39 fused with the first rmsnorm). */
+B2D_API int b2d_embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x,
+                                  const float* gamma, float eps, uint16_t* out, int D, int batch,
+                                  b2d_stream_t stream);
 
 /* x[i] += p[i], fp32, n elements (residual add after a tensor-parallel all-reduce). */
 B2D_API int b2d_add_f32(float* x, const float* p, size_t n, b2d_stream_t stream);

@@ -85,3 +85,29 @@ def test_decode_step_llama_shape_small_batch():
         changed_ref = np.any(b.view(np.uint16) != orig.view(np.uint16), axis=-1)
         np.testing.assert_array_equal(changed_gpu, changed_ref)
         np.testing.assert_allclose(a.astype(np.float32), b.astype(np.float32), rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_decode_step_tensor_core_batch(use_graph):
+    """Batch 24 takes the tcgen05 path (fp16 activation operands, fused norms)."""
+    cfg = S.ModelConfig(2048, 2, 32, 8, 64, 8192, 4096, 1e-5, 500000.0)
+    w = S.synth_weights(cfg, seed=15)
+    r = np.random.default_rng(16)
+    lens = r.integers(0, 1200, size=24).tolist()
+    max_ctx = 1300
+    nblk = sum(-(-(n + 1) // 16) for n in lens) + 4
+    table = make_block_table(lens, -(-max_ctx // 16), nblk, seed=17).numpy()
+    shape = (nblk, cfg.n_kv_heads, 16, cfg.head_dim)
+    kp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
+    vp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
+    tokens = r.integers(0, cfg.vocab, size=len(lens)).tolist()
+    logits, nxt, gk, gv = run_engine(cfg, w, tokens, lens, table, kp, vp, use_graph=use_graph)
+    ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, kp, vp)
+    # each projection's activation operand is fp16 on this path (2^-11 rounding), so the
+    # model-level check is max-normalized, as the reference's own logit check (max |dlogit|
+    # against the logit range, ios_kernels/benchmarking/reference.py:72-80)
+    assert_norm_close(logits, ref_logits, 2e-3, what="tensor-core step logits")
+    np.testing.assert_array_equal(nxt, O.argmax(logits))
+    srt = np.sort(ref_logits, axis=1)
+    safe = (srt[:, -1] - srt[:, -2]) > 2e-3 * np.abs(srt[:, -1])
+    np.testing.assert_array_equal(nxt[safe], ref_next[safe])

@@ -1,0 +1,105 @@
+"""Tensor-core batched GEMV (tcgen05 / TMEM / TMA) against the float64 oracle.
+
+fp16 weights and fp16 activations are exact inputs; the kernel accumulates in fp32 -> 2e-3
+elementwise with a floor (the fp16-path tolerance); split-K sums are deterministic.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from gemmagemini4hackathon2026_10_2425_b200 import ops
+from oracle import ops as O
+from tests._tol import assert_rel_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def case(M, K, b, seed, scale=0.02):
+    r = np.random.default_rng(seed)
+    W = (r.standard_normal((M, K)) * scale).astype(np.float16)
+    X = r.standard_normal((b, K)).astype(np.float16)
+    return W, X
+
+
+def d(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+@pytest.mark.parametrize("M,K", [(3072, 2048), (2048, 2048), (2048, 8192), (4096, 4096), (14336, 4096), (1000, 520), (128, 64), (200, 72)])
+@pytest.mark.parametrize("b", [1, 9, 16, 17, 32])
+def test_tc_store(M, K, b):
+    W, X = case(M, K, b, M + K + b)
+    y = ops.gemm_tc(d(W), d(X)).cpu().numpy()
+    assert_rel_close(y, O.gemv(W, X), 2e-3, what=f"{M}x{K} b{b}")
+
+
+def test_tc_add_fp16_out_and_determinism():
+    W, X = case(2048, 2048, 32, 5)
+    y0 = np.random.default_rng(6).standard_normal((32, 2048)).astype(np.float32)
+    y = d(y0.copy())
+    ops.gemm_tc(d(W), d(X), epilogue="add", y=y)
+    assert_rel_close(y.cpu().numpy(), y0 + O.gemv(W, X), 2e-3)
+    a = ops.gemm_tc(d(W), d(X)).cpu().numpy()
+    b = ops.gemm_tc(d(W), d(X)).cpu().numpy()
+    np.testing.assert_array_equal(a, b)  # fixed-order split-K reduction
+    h = ops.gemm_tc(d(W), d(X), out_dtype=torch.float16)
+    assert h.dtype == torch.float16
+    assert_rel_close(h.float().cpu().numpy(), O.gemv(W, X), 2e-3)
+
+
+@pytest.mark.parametrize("b", [12, 32])
+def test_tc_swiglu(b):
+    Wg, X = case(8192, 2048, b, 7)
+    Wu, _ = case(8192, 2048, b, 8)
+    h = ops.gemm_tc(d(Wg), d(X), epilogue="swiglu", W_up=d(Wu), out_dtype=torch.float16)
+    ref = O.swiglu(O.gemv(Wg, X), O.gemv(Wu, X))
+    assert_rel_close(h.float().cpu().numpy(), ref, 2e-3)
+
+
+def test_tc_gelu_mul():
+    W, X = case(1024, 512, 20, 9)
+    aux = np.random.default_rng(10).standard_normal((20, 1024)).astype(np.float32)
+    y = ops.gemm_tc(d(W), d(X), epilogue="gelu_mul", aux=d(aux))
+    assert_rel_close(y.cpu().numpy(), O.gelu_tanh(O.gemv(W, X)) * aux, 2e-3)
+
+
+@pytest.mark.parametrize("V,b", [(128256, 32), (128256, 16), (5000, 20), (300, 9)])
+def test_tc_argmax(V, b):
+    W, X = case(V, 2048 if V > 1000 else 128, b, V + b)
+    tok, logits = ops.gemm_tc(d(W), d(X), epilogue="argmax", return_logits=True)
+    ref = O.gemv(W, X)
+    lg = logits.cpu().numpy()
+    assert_rel_close(lg, ref, 2e-3)
+    np.testing.assert_array_equal(tok.cpu().numpy(), O.argmax(lg))
+    srt = np.sort(ref, axis=1)
+    safe = (srt[:, -1] - srt[:, -2]) > 1e-3 * np.abs(srt[:, -1])
+    np.testing.assert_array_equal(tok.cpu().numpy()[safe], O.argmax(ref)[safe])
+
+
+def test_tc_argmax_ties_and_offset():
+    W = np.zeros((4096, 64), np.float16)
+    W[[100, 3000, 4095]] = 0.5
+    X = np.ones((10, 64), np.float16)
+    tok = ops.gemm_tc(d(W), d(X), epilogue="argmax", index_offset=7).cpu().numpy()
+    np.testing.assert_array_equal(tok, np.full(10, 107))
+
+
+def test_tc_error_word_stays_zero():
+    W, X = case(2048, 2048, 32, 11)
+    ws = torch.zeros(ops.tc_workspace_bytes(2048, 2048, 32), dtype=torch.uint8, device=DEV)
+    ops.gemm_tc(d(W), d(X), workspace=ws)
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+
+
+def test_add_rmsnorm_f16():
+    r = np.random.default_rng(1)
+    x = r.standard_normal((5, 2048)).astype(np.float32)
+    p = r.standard_normal((5, 2048)).astype(np.float32)
+    g = (1 + 0.1 * r.standard_normal(2048)).astype(np.float32)
+    xt = d(x.copy())
+    out = ops.add_rmsnorm_f16(xt, d(g), 1e-5, p=d(p))
+    np.testing.assert_allclose(xt.cpu().numpy(), x + p, rtol=1e-6)
+    assert_rel_close(out.float().cpu().numpy(), O.rmsnorm(x + p, g, 1e-5), 2e-3)
