@@ -22,6 +22,7 @@
 
 namespace b2d {
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
+size_t attn_ws_header_bytes(int batch, int n_kv_heads);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
                       void*, size_t, cudaStream_t);
@@ -82,8 +83,8 @@ int b2d_paged_decode_attn_noalloc(void* qkv, int qkv_dtype, int ldqkv, uint16_t*
   void* scratch = nullptr;
   B2D_TRY(scratch_for_current_device(&scratch));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // the arrival counters (first bytes of the scratch) must start at zero
-  const size_t counter_bytes = ((size_t)batch * n_kv_heads * sizeof(unsigned int) + 255) / 256 * 256;
+  // the arrival counters and the error word (the scratch's header) must start at zero
+  const size_t counter_bytes = attn_ws_header_bytes(batch, n_kv_heads);
   cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, s);
   if (e != cudaSuccess) {
     set_cuda_error(e);

@@ -16,16 +16,19 @@
 //  * warp 1 / lane 0 issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=16|32, K=16, fp32
 //    accumulate) into TMEM and frees each ring slot with tcgen05.commit;
 //  * all four warps read the accumulator tile back with tcgen05.ld (warp w owns TMEM lanes
-//    32w..32w+31 = W rows), then either finish the epilogue directly (one K split) or write fp32
-//    partials; the last CTA of each row tile (arrival counter) sums the splits in a fixed order
-//    (deterministic) and runs the epilogue: store / residual add / SwiGLU / argmax.
+//    32w..32w+31 = W rows), then finish the epilogue (store / residual add / SwiGLU / argmax);
+//  * split-K: the K splits of a row tile run as one thread-block cluster (<= 8 CTAs); partial
+//    tiles meet in distributed shared memory and each CTA reduces a slice of rows over its
+//    peers in a fixed order (deterministic, no global round trip).
 //  * every mbarrier wait is bounded by a clock64 budget; on timeout the CTA records an error
 //    word in the workspace, skips the rest and still releases its TMEM.
+#include <cooperative_groups.h>
 #include <cuda.h>
 
 #include <algorithm>
 #include <mutex>
 
+#include "async.cuh"
 #include "common.cuh"
 
 namespace b2d {
@@ -35,7 +38,6 @@ namespace tc {
 constexpr int BM = 128;        // W rows per tile (MMA M)
 constexpr int BK = 64;         // K elements per stage (128 bytes of fp16 = one swizzle row)
 constexpr int THREADS = 128;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz: bounded waits
 
 enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_DONE = 3 };
 
@@ -50,8 +52,6 @@ struct Params {
   int y_f16;
   int ldy;
   const float* aux;
-  float* partials;           // [m_tiles][k_splits][nacc][BM][N]
-  unsigned int* counters;    // [m_tiles]
   int* err;                  // error word
   // argmax
   float* logits;             // optional [batch][M] (ld = ldy)
@@ -62,54 +62,6 @@ struct Params {
   int* am_idx;
   unsigned int* am_counter;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false (and the error word set) if the phase did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* err, int code) {
-  if (mbar_try_wait(bar, phase)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, phase)) {
-    if (clock64() - t0 > kWaitCycles) {
-      atomicCAS(err, 0, code);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
@@ -181,7 +133,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
   static constexpr int B_BYTES = N * BK * 2;           // 2 / 4 KB
   static constexpr int STAGE_BYTES = A_BYTES * (DUAL ? 2 : 1) + B_BYTES;
-  static constexpr int STAGES = DUAL ? 5 : 8;
+  static constexpr int STAGES = DUAL ? 5 : 8;  // one CTA per SM, deep TMA ring
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;  // + alignment slack
   static constexpr int NACC = DUAL ? 2 : 1;
   static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
@@ -306,55 +258,70 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(C::TMEM_COLS));
   }
-  if (!have || abort_flag) return;
-  pdl_wait();  // epilogue reads / writes buffers the previous kernel may touch
-  pdl_launch_dependents();
-
-  const int r = warp * 32 + lane;  // row within the tile
+  const bool ok = have && !abort_flag;  // CTA-uniform
+  const int r = warp * 32 + lane;        // row within the tile
   const int row = m0 + r;
 
   if (p.k_splits > 1) {
-    float* mine = p.partials + (((size_t)m_tile * p.k_splits + split) * C::NACC) * BM * N;
+    // Split-K through the thread-block cluster: the k_splits CTAs of this row tile form one
+    // cluster.  Each parks its fp32 partial tile in its own (now idle) ring memory, then
+    // reduces a slice of rows over all peers' tiles through distributed shared memory, in
+    // peer order (deterministic), and runs the epilogue for that slice.  Every CTA takes
+    // both cluster barriers, also on the error path.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    constexpr int LDR = BM + 4;  // token-major [N][BM + 4]: conflict-free row writes
+    float* red = reinterpret_cast<float*>(smem);
+    if (ok) {
 #pragma unroll
-    for (int t = 0; t < N; t += 4) {
-      *reinterpret_cast<float4*>(mine + (size_t)r * N + t) =
-          make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
-      if (DUAL)
-        *reinterpret_cast<float4*>(mine + (size_t)BM * N + (size_t)r * N + t) =
-            make_float4(acc2[t], acc2[t + 1], acc2[t + 2], acc2[t + 3]);
+      for (int t = 0; t < N; ++t) {
+        red[t * LDR + r] = acc[t];
+        if (DUAL) red[N * LDR + t * LDR + r] = acc2[t];
+      }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(p.counters + m_tile, 1u) == (unsigned)(p.k_splits - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-#pragma unroll
-    for (int t = 0; t < N; ++t) {
-      acc[t] = 0.f;
-      if (DUAL) acc2[t] = 0.f;
-    }
-    for (int sp = 0; sp < p.k_splits; ++sp) {  // fixed order: deterministic sums
-      const float* src = p.partials + (((size_t)m_tile * p.k_splits + sp) * C::NACC) * BM * N;
-#pragma unroll
-      for (int t = 0; t < N; t += 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (size_t)r * N + t));
-        acc[t] += v.x;
-        acc[t + 1] += v.y;
-        acc[t + 2] += v.z;
-        acc[t + 3] += v.w;
-        if (DUAL) {
-          const float4 u =
-              __ldcg(reinterpret_cast<const float4*>(src + (size_t)BM * N + (size_t)r * N + t));
-          acc2[t] += u.x;
-          acc2[t + 1] += u.y;
-          acc2[t + 2] += u.z;
-          acc2[t + 3] += u.w;
+    cl.sync();
+    pdl_wait();
+    pdl_launch_dependents();
+    const int ks = p.k_splits;
+    const int rank = (int)cl.block_rank();
+    const int lo = rank * BM / ks, hi = (rank + 1) * BM / ks, span = hi - lo;
+    if (ok) {
+      for (int v = tid; v < span * N; v += THREADS) {
+        const int rr = lo + v % span, t = v / span;
+        float a = 0.f, a2 = 0.f;
+        for (int q = 0; q < ks; ++q) {
+          const float* peer = cl.map_shared_rank(red, q);
+          a += peer[t * LDR + rr];
+          if (DUAL) a2 += peer[N * LDR + t * LDR + rr];
+        }
+        const int grow = m0 + rr;
+        if (t < p.batch && grow < p.M) {
+          const size_t yi = (size_t)t * p.ldy + grow;
+          float y;
+          if (DUAL) {
+            y = silu(a) * a2;
+          } else {
+            y = a;
+            if (p.epi == B2D_EPI_ADD)
+              y += p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
+                           : reinterpret_cast<const float*>(p.y)[yi];
+            else if (p.epi == B2D_EPI_GELU_MUL)
+              y = gelu_tanh(y) * p.aux[yi];
+          }
+          if (p.y_f16)
+            reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
+          else
+            reinterpret_cast<float*>(p.y)[yi] = y;
         }
       }
     }
-    if (tid == 0) p.counters[m_tile] = 0u;  // ready for the next launch
+    cl.sync();  // peers keep their shared memory until every slice has been read
+    return;
   }
+
+  if (!ok) return;
+  pdl_wait();  // epilogue reads / writes buffers the previous kernel may touch
+  pdl_launch_dependents();
 
   if constexpr (ARGMAX) {
     // logits (optional), then per-token (max, row) over this tile
@@ -456,7 +423,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2D fp16 tensor [rows, cols] with row stride ld (elements), box {64, box_rows}, 128B swizzle.
-static int make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows) {
+int make_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, int cols, int ld,
+                  int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return B2D_ERR_CUDA;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -469,9 +437,12 @@ static int make_map(CUtensorMap* m, const void* base, int rows, int cols, int ld
   return r == CUDA_SUCCESS ? B2D_OK : B2D_ERR_ALIGN;
 }
 
+constexpr int kMaxTiles = 4096;  // row tiles per call: M <= 4096 * 128
+constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
+
 struct TcPlan {
   int n_tile, m_tiles, k_tiles, k_splits, nacc;
-  size_t off_counters, off_partials, off_amv, off_ami, total;
+  size_t off_amv, off_ami, total;
 };
 
 static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
@@ -482,15 +453,13 @@ static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
   pl.nacc = epilogue == B2D_EPI_SWIGLU ? 2 : 1;
   if (epilogue == B2D_EPI_ARGMAX) {
     pl.k_splits = 1;
-  } else {
-    pl.k_splits = std::max(1, std::min(num_sms() / pl.m_tiles, std::min(pl.k_tiles, 16)));
+  } else {  // one wave of clusters: k_splits CTAs per row tile, one CTA per SM
+    pl.k_splits =
+        std::max(1, std::min(num_sms() / pl.m_tiles, std::min(pl.k_tiles, kMaxClusterSplits)));
   }
   auto a256 = [](size_t n) { return (n + 255) / 256 * 256; };
-  size_t o = 256;  // [0]: error word, [64]: argmax arrival counter
-  pl.off_counters = o;
-  o += a256((size_t)pl.m_tiles * 4);
-  pl.off_partials = o;
-  if (pl.k_splits > 1) o += a256((size_t)pl.m_tiles * pl.k_splits * pl.nacc * tc::BM * pl.n_tile * 4);
+  // [0] error word, [64] argmax arrival counter, [256...) argmax partials (value, index)
+  size_t o = 256;
   pl.off_amv = o;
   pl.off_ami = o;
   if (epilogue == B2D_EPI_ARGMAX) {
@@ -503,7 +472,7 @@ static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
 }
 
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue) {
-  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32) return 0;
+  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || M > kMaxTiles * tc::BM) return 0;
   return tc_plan(M, K, batch, epilogue).total;
 }
 
@@ -527,11 +496,19 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
   cfg.blockDim = dim3(tc::THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (grid.y > 1) {  // the K splits of a row tile run as one thread-block cluster
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = grid.y;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, prm);
   if (e != cudaSuccess) {
     set_cuda_error(e);
@@ -555,7 +532,8 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
                     int K, int batch, float* logits, int* tokens, float* max_vals,
                     int index_offset, void* workspace, size_t workspace_bytes) {
   if (!call || !W || !X) return B2D_ERR_NULL;
-  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8)
+  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8 ||
+      M > kMaxTiles * tc::BM)
     return B2D_ERR_SHAPE;
   if (epilogue < B2D_EPI_STORE || epilogue > B2D_EPI_ARGMAX) return B2D_ERR_UNSUPPORTED;
   if (y_dtype != B2D_F32 && y_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
@@ -570,9 +548,9 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   if (!aligned16(workspace)) return B2D_ERR_ALIGN;
   tc::Params& p = call->prm;
   p = tc::Params{};
-  B2D_TRY(make_map(&p.tmA, W, M, K, K, tc::BM));
-  if (W_up) B2D_TRY(make_map(&p.tmA2, W_up, M, K, K, tc::BM));
-  B2D_TRY(make_map(&p.tmB, X, batch, K, ldx, pl.n_tile));
+  B2D_TRY(make_tmap_f16(&p.tmA, W, M, K, K, tc::BM));
+  if (W_up) B2D_TRY(make_tmap_f16(&p.tmA2, W_up, M, K, K, tc::BM));
+  B2D_TRY(make_tmap_f16(&p.tmB, X, batch, K, ldx, pl.n_tile));
   char* ws = static_cast<char*>(workspace);
   p.M = M;
   p.K = K;
@@ -587,8 +565,6 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   p.aux = aux;
   p.err = reinterpret_cast<int*>(ws);
   p.am_counter = reinterpret_cast<unsigned int*>(ws + 64);
-  p.counters = reinterpret_cast<unsigned int*>(ws + pl.off_counters);
-  p.partials = reinterpret_cast<float*>(ws + pl.off_partials);
   p.logits = logits;
   p.tokens = tokens;
   p.max_vals = max_vals;

@@ -159,3 +159,18 @@ def test_out_of_pool_block_ids_are_skipped():
     c["table"][0, 1] = 10**6  # second page: tokens 16..31 become invisible
     go, _, _ = run_gpu(c, 8, 2, 64, 500000.0)
     assert np.all(np.isfinite(go))
+
+
+def test_workspace_shared_across_batch_shapes():
+    """Calls with different (batch, KV heads) share one workspace: counters and partials live
+    in fixed, separate regions."""
+    ws = torch.zeros(ops.attn_workspace_bytes(40, 32, 8, 128, 4100), dtype=torch.uint8, device=DEV)
+    for lens, hq, hk in [([300, 4000], 32, 8), ([3000] * 40, 32, 8), ([50, 2100, 900], 8, 2)]:
+        c = make_case(lens, hq, hk, 128, seed=len(lens) * 7 + hk)
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+        out = ops.paged_decode_attn(
+            dev(c["qkv"]), dev(c["kp"]), dev(c["vp"]), dev(c["table"]), dev(c["lens"]),
+            dev(O.inv_freq(128, 10000.0)), hq, hk, 128, c["max_ctx"], workspace=ws,
+        )
+        ro, _, _ = run_oracle(c, hq, hk, 128, 10000.0)
+        assert_rel_close(out.cpu().numpy(), ro, 2e-3)

@@ -103,3 +103,14 @@ def test_add_rmsnorm_f16():
     out = ops.add_rmsnorm_f16(xt, d(g), 1e-5, p=d(p))
     np.testing.assert_allclose(xt.cpu().numpy(), x + p, rtol=1e-6)
     assert_rel_close(out.float().cpu().numpy(), O.rmsnorm(x + p, g, 1e-5), 2e-3)
+
+
+def test_tc_workspace_shared_across_shapes():
+    """One workspace reused by calls of different shapes (as the decoder does): each call's
+    split-K partials must never land on another call's arrival counters."""
+    nbytes = max(ops.tc_workspace_bytes(M, K, 32, e) for M, K, e in [(4096, 4096, "store"), (14336, 4096, "store"), (8192, 2048, "swiglu"), (128256, 2048, "argmax")])
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    for M, K in [(4096, 4096), (14336, 4096), (2048, 8192), (14336, 4096), (3072, 2048)]:
+        W, X = case(M, K, 32, M * 3 + K)
+        y = ops.gemm_tc(d(W), d(X), workspace=ws).cpu().numpy()
+        assert_rel_close(y, O.gemv(W, X), 2e-3, what=f"shared ws {M}x{K}")
