@@ -40,6 +40,7 @@ constexpr int BK = 64;         // K elements per stage (128 bytes of fp16 = one 
 constexpr int THREADS = 128;
 
 enum { ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_DONE = 3 };
+constexpr int kMaxSplits = 8;  // K splits of a row tile = CTAs of one (portable) cluster
 
 struct Params {
   CUtensorMap tmA;   // W      [M, K] fp16, box {64, 128}, 128B swizzle
@@ -133,9 +134,12 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
   static constexpr int B_BYTES = N * BK * 2;           // 2 / 4 KB
   static constexpr int STAGE_BYTES = A_BYTES * (DUAL ? 2 : 1) + B_BYTES;
-  static constexpr int STAGES = DUAL ? 5 : 8;  // one CTA per SM, deep TMA ring
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+  static constexpr int STAGES = DUAL ? 4 : 8;  // one CTA per SM, deep TMA ring
   static constexpr int NACC = DUAL ? 2 : 1;
+  // split-K receive buffer (not aliased with the ring: peers write into it while this CTA may
+  // still be streaming): [source rank][acc][token][owned rows + pad], owned rows = BM / splits
+  static constexpr int RED_FLOATS = NACC * N * (BM + 4 * 8);
+  static constexpr int SMEM = STAGES * STAGE_BYTES + RED_FLOATS * 4 + 1024;  // + alignment
   static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
 };
 
@@ -161,6 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const int kt_end = (int)((long long)(split + 1) * p.k_tiles / p.k_splits);
   const int nkt = kt_end - kt_begin;
 
+  const int first = min(nkt, C::STAGES);
   if (tid == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -169,9 +174,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_flag = 0;
-    tma_prefetch_desc(&p.tmA);
-    if (DUAL) tma_prefetch_desc(&p.tmA2);
-    tma_prefetch_desc(&p.tmB);
+    // weight tiles do not depend on the previous kernel: start streaming them at once
+    for (int i = 0; i < first; ++i) {
+      uint8_t* st = smem + i * C::STAGE_BYTES;
+      mbar_expect_tx(&full_bar[i], C::STAGE_BYTES);
+      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
+      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
+    }
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -183,17 +192,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  // split-K clusters: announce that this CTA runs (peers write into its shared memory later)
+  if (p.k_splits > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
     const uint32_t tx = C::STAGE_BYTES;
-    const int first = min(nkt, C::STAGES);
-    for (int i = 0; i < first; ++i) {  // weight tiles: independent of the previous kernel
-      uint8_t* st = smem + i * C::STAGE_BYTES;
-      mbar_expect_tx(&full_bar[i], tx);
-      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
-      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
-    }
     pdl_wait();  // activations come from the previous kernel
     for (int i = 0; i < first; ++i) {
       uint8_t* st = smem + i * C::STAGE_BYTES;
@@ -264,58 +268,82 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 
   if (p.k_splits > 1) {
     // Split-K through the thread-block cluster: the k_splits CTAs of this row tile form one
-    // cluster.  Each parks its fp32 partial tile in its own (now idle) ring memory, then
-    // reduces a slice of rows over all peers' tiles through distributed shared memory, in
-    // peer order (deterministic), and runs the epilogue for that slice.  Every CTA takes
-    // both cluster barriers, also on the error path.
+    // cluster.  Rows are owned in 16-row slices (slice s by rank s % k_splits).  Each CTA
+    // stores its partial rows straight into the owners' receive buffers (distributed shared
+    // memory), one cluster barrier publishes them, and every owner sums its rows over the
+    // sources in rank order (deterministic) from local shared memory, then runs the epilogue.
+    // No CTA touches a peer's memory after the barrier, so one barrier suffices.
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
-    constexpr int LDR = BM + 4;  // token-major [N][BM + 4]: conflict-free row writes
-    float* red = reinterpret_cast<float*>(smem);
-    if (ok) {
-#pragma unroll
-      for (int t = 0; t < N; ++t) {
-        red[t * LDR + r] = acc[t];
-        if (DUAL) red[N * LDR + t * LDR + r] = acc2[t];
-      }
-    }
-    cl.sync();
-    pdl_wait();
-    pdl_launch_dependents();
     const int ks = p.k_splits;
     const int rank = (int)cl.block_rank();
-    const int lo = rank * BM / ks, hi = (rank + 1) * BM / ks, span = hi - lo;
+    const int own_rows = BM / ks;
+    const int old_ = own_rows + 4;  // padded row stride of the receive buffer
+    float* red = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every peer has started
     if (ok) {
-      for (int v = tid; v < span * N; v += THREADS) {
-        const int rr = lo + v % span, t = v / span;
-        float a = 0.f, a2 = 0.f;
-        for (int q = 0; q < ks; ++q) {
-          const float* peer = cl.map_shared_rank(red, q);
-          a += peer[t * LDR + rr];
-          if (DUAL) a2 += peer[N * LDR + t * LDR + rr];
-        }
-        const int grow = m0 + rr;
-        if (t < p.batch && grow < p.M) {
-          const size_t yi = (size_t)t * p.ldy + grow;
-          float y;
-          if (DUAL) {
-            y = silu(a) * a2;
-          } else {
-            y = a;
-            if (p.epi == B2D_EPI_ADD)
-              y += p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
-                           : reinterpret_cast<const float*>(p.y)[yi];
-            else if (p.epi == B2D_EPI_GELU_MUL)
-              y = gelu_tanh(y) * p.aux[yi];
+      const int sl = r / 16, owner = sl % ks;
+      const int lr = (sl / ks) * 16 + (r % 16);
+      float* dst = cl.map_shared_rank(red, owner);
+#pragma unroll
+      for (int t = 0; t < N; ++t) {
+        dst[((rank * C::NACC + 0) * N + t) * old_ + lr] = acc[t];
+        if (DUAL) dst[((rank * C::NACC + 1) * N + t) * old_ + lr] = acc2[t];
+      }
+    }
+    // prefetch what the epilogue reads from global memory while the barrier completes
+    constexpr int MAXV = N / 2;  // values per thread for k_splits >= 2
+    float yv[DUAL ? 1 : MAXV];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int nv = own_rows * N;
+    if (!DUAL && ok && (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL)) {
+#pragma unroll
+      for (int k = 0; k < MAXV; ++k) {
+        const int v = tid + k * THREADS;
+        yv[k] = 0.f;
+        if (v < nv) {
+          const int lr = v % own_rows, t = v / own_rows;
+          const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
+          if (t < p.batch && grow < p.M) {
+            const size_t yi = (size_t)t * p.ldy + grow;
+            yv[k] = p.epi == B2D_EPI_GELU_MUL
+                        ? p.aux[yi]
+                        : (p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
+                                   : reinterpret_cast<const float*>(p.y)[yi]);
           }
-          if (p.y_f16)
-            reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
-          else
-            reinterpret_cast<float*>(p.y)[yi] = y;
         }
       }
     }
-    cl.sync();  // peers keep their shared memory until every slice has been read
+    cl.sync();  // every partial row has reached its owner
+    if (ok) {
+#pragma unroll
+      for (int k = 0; k < MAXV; ++k) {
+        const int v = tid + k * THREADS;
+        if (v >= nv) break;
+        const int lr = v % own_rows, t = v / own_rows;
+        const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
+        float a = 0.f, a2 = 0.f;
+        for (int q = 0; q < ks; ++q) {  // fixed source order: deterministic sums
+          a += red[((q * C::NACC + 0) * N + t) * old_ + lr];
+          if (DUAL) a2 += red[((q * C::NACC + 1) * N + t) * old_ + lr];
+        }
+        if (t >= p.batch || grow >= p.M) continue;
+        const size_t yi = (size_t)t * p.ldy + grow;
+        float y;
+        if (DUAL) {
+          y = silu(a) * a2;
+        } else {
+          y = a;
+          if (p.epi == B2D_EPI_ADD) y += yv[k];
+          else if (p.epi == B2D_EPI_GELU_MUL) y = gelu_tanh(y) * yv[k];
+        }
+        if (p.y_f16)
+          reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
+        else
+          reinterpret_cast<float*>(p.y)[yi] = y;
+      }
+    }
     return;
   }
 
@@ -438,7 +466,6 @@ int make_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, int cols, int
 }
 
 constexpr int kMaxTiles = 4096;  // row tiles per call: M <= 4096 * 128
-constexpr int kMaxClusterSplits = 8;  // portable thread-block cluster size
 
 struct TcPlan {
   int n_tile, m_tiles, k_tiles, k_splits, nacc;
@@ -451,12 +478,7 @@ static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
   pl.m_tiles = (M + tc::BM - 1) / tc::BM;
   pl.k_tiles = (K + tc::BK - 1) / tc::BK;
   pl.nacc = epilogue == B2D_EPI_SWIGLU ? 2 : 1;
-  if (epilogue == B2D_EPI_ARGMAX) {
-    pl.k_splits = 1;
-  } else {  // one wave of clusters: k_splits CTAs per row tile, one CTA per SM
-    pl.k_splits =
-        std::max(1, std::min(num_sms() / pl.m_tiles, std::min(pl.k_tiles, kMaxClusterSplits)));
-  }
+  pl.k_splits = 1;  // chosen at launch (tc_pick_splits): it depends on cluster residency
   auto a256 = [](size_t n) { return (n + 255) / 256 * 256; };
   // [0] error word, [64] argmax arrival counter, [256...) argmax partials (value, index)
   size_t o = 256;
@@ -518,6 +540,47 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
   return B2D_OK;
 }
 
+// K splits (= cluster size) for a row-tile count: the largest power of two <= 8 whose clusters
+// all fit on the GPU in one wave (cudaOccupancyMaxActiveClusters for this kernel), without
+// more CTAs than SMs and without splitting K below one 64-wide tile.
+template <int N, bool DUAL>
+static int tc_pick_splits(int m_tiles, int k_tiles) {
+  using C = tc::Cfg<N, DUAL>;
+  auto kern = tc::tc_gemm_kernel<N, DUAL, false>;
+  static int cached_dev = -1;
+  static int max_clusters[4] = {0, 0, 0, 0};  // cluster sizes 1, 2, 4, 8
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cached_dev != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    for (int i = 0; i < 4; ++i) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1 << i);
+      cfg.blockDim = dim3(tc::THREADS);
+      cfg.dynamicSmemBytes = C::SMEM;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = 1 << i;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = i == 0 ? num_sms() : 0;
+      }
+      max_clusters[i] = n;
+    }
+    cached_dev = dev;
+  }
+  for (int i = 3; i >= 1; --i) {
+    const int ks = 1 << i;
+    if (ks <= k_tiles && m_tiles * ks <= num_sms() && m_tiles <= max_clusters[i]) return ks;
+  }
+  return 1;
+}
+
 // A prepared call: tensor maps encoded once, reusable (and graph-capturable) while the
 // pointers stay the same.
 struct TcCall {
@@ -571,7 +634,14 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   p.index_offset = index_offset;
   p.am_val = reinterpret_cast<float*>(ws + pl.off_amv);
   p.am_idx = reinterpret_cast<int*>(ws + pl.off_ami);
-  call->grid = dim3(pl.m_tiles, pl.k_splits);
+  if (epilogue != B2D_EPI_ARGMAX) {
+    const bool dual = epilogue == B2D_EPI_SWIGLU;
+    p.k_splits = pl.n_tile == 16 ? (dual ? tc_pick_splits<16, true>(pl.m_tiles, pl.k_tiles)
+                                         : tc_pick_splits<16, false>(pl.m_tiles, pl.k_tiles))
+                                 : (dual ? tc_pick_splits<32, true>(pl.m_tiles, pl.k_tiles)
+                                         : tc_pick_splits<32, false>(pl.m_tiles, pl.k_tiles));
+  }
+  call->grid = dim3(pl.m_tiles, p.k_splits);
   call->n_tile = pl.n_tile;
   call->dual = epilogue == B2D_EPI_SWIGLU;
   call->argmax = epilogue == B2D_EPI_ARGMAX;

@@ -1,0 +1,103 @@
+"""Tensor-parallel decode step on 2 GPUs (NCCL) against the single-GPU oracle.
+
+Runs only where at least two GPUs are visible; each rank is a spawned process that builds its
+DecodeEngine shard, runs one step (CUDA-core path at batch 5, tensor-core path at batch 24)
+and sends its vocab-shard logits and the combined next tokens back to the test.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _case(batch):
+    from gemmagemini4hackathon2026_10_2425_b200.engine import make_block_table
+    from oracle import step as S
+
+    cfg = S.ModelConfig(2048, 2, 32, 8, 64, 8192, 4096, 1e-5, 500000.0)
+    w = S.synth_weights(cfg, seed=21)
+    r = np.random.default_rng(22 + batch)
+    lens = r.integers(0, 900, size=batch).tolist()
+    max_ctx = 1024
+    nblk = sum(-(-(n + 1) // 16) for n in lens) + 4
+    table = make_block_table(lens, max_ctx // 16, nblk, seed=23).numpy()
+    shape = (nblk, cfg.n_kv_heads, 16, cfg.head_dim)
+    kp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
+    vp = [r.standard_normal(shape).astype(np.float16) for _ in range(cfg.n_layers)]
+    tokens = r.integers(0, cfg.vocab, size=batch).tolist()
+    return cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens
+
+
+def _rank(rank, world, port, batch, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, share_nccl_id
+    from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens = _case(batch)
+        shape = ModelShape(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
+        eng = DecodeEngine(shape, max_batch=batch, max_ctx=max_ctx, n_blocks=nblk, tp_rank=rank, tp_size=world, nccl_id=share_nccl_id(rank), device=dev)
+        eng.alloc_kv()
+        hk = cfg.n_kv_heads // world
+        for i in range(cfg.n_layers):  # this rank's KV heads
+            eng.k_pages[i].copy_(torch.from_numpy(np.ascontiguousarray(kp[i][:, rank * hk : (rank + 1) * hk])))
+            eng.v_pages[i].copy_(torch.from_numpy(np.ascontiguousarray(vp[i][:, rank * hk : (rank + 1) * hk])))
+        eng.load_weights({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()})
+        i32 = lambda a: torch.tensor(np.asarray(a, np.int32), device=dev)
+        tok, ln, tb = i32(tokens), i32(lens), torch.from_numpy(table).to(dev)
+        nxt = torch.empty_like(tok)
+        logits = torch.empty(batch, eng.lm_rows, dtype=torch.float32, device=dev)
+        eng.step(tok, ln, tb, nxt, logits, use_graph=True)
+        eng.step(tok, ln, tb, nxt, logits, use_graph=True)  # replay
+        eng.stream.synchronize()
+        q.put((rank, logits.cpu().numpy(), nxt.cpu().numpy()))
+        eng.close()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("batch", [5, 24])
+@pytest.mark.timeout(600)
+def test_tp2_decode_step_matches_oracle(batch):
+    from oracle import step as S
+    from tests._tol import assert_norm_close
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, lg, nx = q.get(timeout=500)
+        got[rank] = (lg, nx)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens = _case(batch)
+    ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, kp, vp)
+    logits = np.concatenate([got[0][0], got[1][0]], axis=1)
+    assert_norm_close(logits, ref_logits, 2e-3, what=f"tp2 logits b{batch}")
+    np.testing.assert_array_equal(got[0][1], got[1][1])  # every rank agrees on the tokens
+    np.testing.assert_array_equal(got[0][1], np.argmax(logits, axis=1))
