@@ -310,7 +310,11 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
                     continue
                 x = torch.randn(bsz, K, generator=g, device=dev).half()
                 y = torch.empty(bsz, M, device=dev)
-                ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
+                if bsz >= 9:  # tensor-core path: raw tiles dequantized in shared memory
+                    wsq = torch.zeros(ops.tc_workspace_bytes(M, K, bsz), dtype=torch.uint8, device=dev)
+                    ms = time_launches(lambda i: ops.gemm_tc_q(Wq[i % n], x, y=y, workspace=wsq), nit(100), s)
+                else:
+                    ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
                 b = wbytes + bsz * K * 2 + bsz * M * 4
                 res[f"c3_{fmt}_{K}to{M}_b{bsz}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
             del Wq

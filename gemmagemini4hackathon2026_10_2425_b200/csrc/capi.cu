@@ -47,6 +47,8 @@ int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, 
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
+int tc_gemm_q(int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+              const float*, int, int, int, void*, size_t, cudaStream_t);
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
@@ -178,6 +180,13 @@ int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int 
                 size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm(W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits, tokens,
                  max_vals, index_offset, workspace, workspace_bytes, S(stream));
+}
+
+int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X, int ldx,
+                  int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
+                  int batch, void* workspace, size_t workspace_bytes, b2d_stream_t stream) {
+  return tc_gemm_q(w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
+                   workspace, workspace_bytes, S(stream));
 }
 
 int b2d_inv_freq(int head_dim, double theta, float* out_host) {

@@ -62,6 +62,7 @@ struct Params {
   float* am_val;             // [m_tiles][N]
   int* am_idx;
   unsigned int* am_counter;
+  const uint16_t* scales;    // quantized weights: fp16 [M, K/32]
 };
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
@@ -129,28 +130,49 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) {
   tmem_ld<16>(taddr + 16, v + 16);
 }
 
-template <int N, bool DUAL>
+// QUANT: 0 = fp16 weights (TMA straight into the MMA operand), 1 = q8_32, 2 = q4_32 (TMA
+// streams the raw tiles; four dequant warps expand them into the fp16 operand).
+constexpr int threads_for(int quant) { return quant ? 192 : 128; }
+
+template <int N, bool DUAL, int QUANT = 0>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
   static constexpr int B_BYTES = N * BK * 2;           // 2 / 4 KB
-  static constexpr int STAGE_BYTES = A_BYTES * (DUAL ? 2 : 1) + B_BYTES;
+  static constexpr int B_OFF = A_BYTES * (DUAL ? 2 : 1);
+  // fp16 weights: one ring of STAGES x [A | (A_up) | B], filled by TMA
+  static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
   static constexpr int STAGES = DUAL ? 4 : 8;  // one CTA per SM, deep TMA ring
+  // quantized weights: a deep ring of RS raw tiles (the HBM stream) and a shallow ring of AS
+  // operand stages [A fp16 | B] that the dequant warps fill
+  static constexpr int RAW_ROW = QUANT == 1 ? BK : (QUANT == 2 ? BK / 2 : 0);  // bytes per row
+  static constexpr int RAW_BYTES = BM * RAW_ROW;  // 8 KB (q8) / 4 KB (q4)
+  static constexpr int RS = QUANT == 1 ? 12 : (QUANT == 2 ? 24 : 1);
+  static constexpr int AS = 3;
+  static constexpr int RAW_RING_OFF = AS * STAGE_BYTES;
+  static constexpr int RING_BYTES = QUANT ? RAW_RING_OFF + RS * RAW_BYTES : STAGES * STAGE_BYTES;
   static constexpr int NACC = DUAL ? 2 : 1;
   // split-K receive buffer (not aliased with the ring: peers write into it while this CTA may
   // still be streaming): [source rank][acc][token][owned rows + pad], owned rows = BM / splits
   static constexpr int RED_FLOATS = NACC * N * (BM + 4 * 8);
-  static constexpr int SMEM = STAGES * STAGE_BYTES + RED_FLOATS * 4 + 1024;  // + alignment
+  static constexpr int SMEM = RING_BYTES + RED_FLOATS * 4 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
 };
 
-template <int N, bool DUAL, bool ARGMAX>
-__global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<N, DUAL>;
+template <int N, bool DUAL, bool ARGMAX, int QUANT = 0>
+__global__ void __launch_bounds__(threads_for(QUANT), 1)
+    tc_gemm_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<N, DUAL, QUANT>;
+  constexpr int EPI0 = QUANT ? 2 : 0;  // first epilogue warp (epilogue warps hold TMEM quarters)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  // quantized pipeline: raw ring (TMA -> dequant) and operand ring (dequant + TMA(B) -> MMA)
+  __shared__ __align__(8) uint64_t raw_full[QUANT ? C::RS : 1];
+  __shared__ __align__(8) uint64_t raw_empty[QUANT ? C::RS : 1];
+  __shared__ __align__(8) uint64_t a_full[QUANT ? C::AS : 1];
+  __shared__ __align__(8) uint64_t a_empty[QUANT ? C::AS : 1];
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -167,19 +189,38 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 
   const int first = min(nkt, C::STAGES);
   if (tid == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+    if constexpr (QUANT) {
+      for (int s = 0; s < C::RS; ++s) {
+        mbar_init(&raw_full[s], 1);
+        mbar_init(&raw_empty[s], 4);  // one arrival per dequant warp
+      }
+      for (int s = 0; s < C::AS; ++s) {
+        mbar_init(&a_full[s], 5);  // 4 dequant warps + the producer's B copy
+        mbar_init(&a_empty[s], 1);
+      }
+    } else {
+      for (int s = 0; s < C::STAGES; ++s) {
+        mbar_init(&full_bar[s], 1);
+        mbar_init(&empty_bar[s], 1);
+      }
     }
     mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     abort_flag = 0;
     // weight tiles do not depend on the previous kernel: start streaming them at once
-    for (int i = 0; i < first; ++i) {
-      uint8_t* st = smem + i * C::STAGE_BYTES;
-      mbar_expect_tx(&full_bar[i], C::STAGE_BYTES);
-      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
-      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
+    if constexpr (QUANT) {
+      for (int i = 0; i < min(nkt, C::RS); ++i) {
+        mbar_expect_tx(&raw_full[i], C::RAW_BYTES);
+        tma_load_2d(smem + C::RAW_RING_OFF + i * C::RAW_BYTES, &p.tmA,
+                    (kt_begin + i) * C::RAW_ROW, m0, &raw_full[i]);
+      }
+    } else {
+      for (int i = 0; i < first; ++i) {
+        uint8_t* st = smem + i * C::STAGE_BYTES;
+        mbar_expect_tx(&full_bar[i], C::STAGE_BYTES);
+        tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
+        if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
+      }
     }
   }
   if (warp == 0) {
@@ -197,38 +238,64 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer ----------------
-    const uint32_t tx = C::STAGE_BYTES;
     pdl_wait();  // activations come from the previous kernel
-    for (int i = 0; i < first; ++i) {
-      uint8_t* st = smem + i * C::STAGE_BYTES;
-      tma_load_2d(st + C::A_BYTES * C::NACC, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[i]);
-    }
-    for (int i = first; i < nkt; ++i) {
-      const int s = i % C::STAGES;
-      if (!mbar_wait(&empty_bar[s], ((i / C::STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-        abort_flag = 1;
-        break;
+    if constexpr (QUANT) {
+      for (int i = 0; i < nkt; ++i) {
+        const int as = i % C::AS;
+        if (i >= C::AS &&
+            !mbar_wait(&a_empty[as], ((i / C::AS) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+          abort_flag = 1;
+          break;
+        }
+        mbar_expect_tx(&a_full[as], C::B_BYTES);
+        tma_load_2d(smem + as * C::STAGE_BYTES + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0,
+                    &a_full[as]);
+        const int j = i + C::RS;  // raw tile that reuses the slot k-tile i is draining
+        if (j < nkt) {
+          const int rs = i % C::RS;
+          if (!mbar_wait(&raw_empty[rs], (i / C::RS) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+            abort_flag = 1;
+            break;
+          }
+          mbar_expect_tx(&raw_full[rs], C::RAW_BYTES);
+          tma_load_2d(smem + C::RAW_RING_OFF + rs * C::RAW_BYTES, &p.tmA,
+                      (kt_begin + j) * C::RAW_ROW, m0, &raw_full[rs]);
+        }
       }
-      uint8_t* st = smem + s * C::STAGE_BYTES;
-      mbar_expect_tx(&full_bar[s], tx);
-      tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[s]);
-      if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[s]);
-      tma_load_2d(st + C::A_BYTES * C::NACC, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[s]);
+    } else {
+      for (int i = 0; i < first; ++i) {
+        uint8_t* st = smem + i * C::STAGE_BYTES;
+        tma_load_2d(st + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[i]);
+      }
+      for (int i = first; i < nkt; ++i) {
+        const int s = i % C::STAGES;
+        if (!mbar_wait(&empty_bar[s], ((i / C::STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+          abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * C::STAGE_BYTES;
+        mbar_expect_tx(&full_bar[s], C::STAGE_BYTES);
+        tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[s]);
+        if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[s]);
+        tma_load_2d(st + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[s]);
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = idesc_f16<N>();
     bool ok = true;
     for (int i = 0; i < nkt; ++i) {
-      const int s = i % C::STAGES;
-      if (!mbar_wait(&full_bar[s], (i / C::STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) {
+      const int s = QUANT ? i % C::AS : i % C::STAGES;
+      const int ph = QUANT ? (i / C::AS) & 1 : (i / C::STAGES) & 1;
+      uint64_t* ready = QUANT ? &a_full[s] : &full_bar[s];
+      if (!mbar_wait(ready, ph, p.err, ERR_TIMEOUT_FULL)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint8_t* st = smem + s * C::STAGE_BYTES;
       const uint64_t a = smem_desc_sw128(st);
-      const uint64_t b = smem_desc_sw128(st + C::A_BYTES * C::NACC);
+      const uint64_t b = smem_desc_sw128(st + C::B_OFF);
 #pragma unroll
       for (int k = 0; k < BK / 16; ++k) {  // 32 bytes of K per MMA: +2 in the 16-byte address field
         const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
@@ -238,10 +305,105 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           mma_f16(tmem + N, a2 + 2 * k, b + 2 * k, idesc, acc);
         }
       }
-      mma_commit(&empty_bar[s]);  // slot is free once these MMAs have read it
+      mma_commit(QUANT ? &a_empty[s] : &empty_bar[s]);  // slot free once these MMAs read it
     }
     if (ok) mma_commit(&done_bar);
     else abort_flag = 1;
+  } else if (QUANT && warp >= 2) {
+    // ---------------- dequantizers: one thread per weight row of the tile ----------------
+    const int dr = (warp - 2) * 32 + lane;
+    const int grow = m0 + dr;
+    const int nsb = p.K / 32;  // scale blocks per row
+    const uint16_t* srow = p.scales + (size_t)min(grow, p.M - 1) * nsb;
+    auto scale_pair = [&](int kt) -> uint32_t {  // fp16 scales of blocks 2kt, 2kt+1 (0 outside)
+      if (grow >= p.M) return 0u;
+      const uint32_t s0 = 2 * kt < nsb ? (uint32_t)__ldg(srow + 2 * kt) : 0u;
+      const uint32_t s1 = 2 * kt + 1 < nsb ? (uint32_t)__ldg(srow + 2 * kt + 1) : 0u;
+      return s0 | (s1 << 16);
+    };
+    uint32_t sc_next = scale_pair(kt_begin);
+    for (int i = 0; i < nkt; ++i) {
+      const int rs = i % C::RS, as = i % C::AS;
+      const uint32_t sc = sc_next;
+      if (i + 1 < nkt) sc_next = scale_pair(kt_begin + i + 1);
+      if (!mbar_wait(&raw_full[rs], (i / C::RS) & 1, p.err, ERR_TIMEOUT_FULL) ||
+          (i >= C::AS &&
+           !mbar_wait(&a_empty[as], ((i / C::AS) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))) {
+        abort_flag = 1;
+        break;
+      }
+      const uint8_t* raw = smem + C::RAW_RING_OFF + rs * C::RAW_BYTES + dr * C::RAW_ROW;
+      uint8_t* arow = smem + as * C::STAGE_BYTES + (dr >> 3) * 1024 + (dr & 7) * 128;  // SW128
+      const __half2 s_lo = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
+      const __half2 s_hi = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
+      if (QUANT == 1) {
+        const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {  // 16-byte raw chunks, rotated by row (bank spread)
+          const int c = (cc + dr) & 3;
+          const uint4 w = *reinterpret_cast<const uint4*>(raw + c * 16);
+          const __half2 sc2 = c < 2 ? s_lo : s_hi;
+          const uint32_t wv[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u,
+                                  w.w ^ 0x80808080u};
+          uint32_t out[8];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // byte b -> fp16 (1024 + b) - 1152 = q, then * scale
+            uint32_t lo = __byte_perm(wv[j], 0x64646464u, 0x4140);
+            uint32_t hi = __byte_perm(wv[j], 0x64646464u, 0x4342);
+            __half2 hl = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), sc2);
+            __half2 hh = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), sc2);
+            out[2 * j] = *reinterpret_cast<uint32_t*>(&hl);
+            out[2 * j + 1] = *reinterpret_cast<uint32_t*>(&hh);
+          }
+          const int o0 = 2 * c, o1 = 2 * c + 1;  // output 8-element chunks
+          *reinterpret_cast<uint4*>(arow + ((o0 ^ (dr & 7)) << 4)) =
+              make_uint4(out[0], out[1], out[2], out[3]);
+          *reinterpret_cast<uint4*>(arow + ((o1 ^ (dr & 7)) << 4)) =
+              make_uint4(out[4], out[5], out[6], out[7]);
+        }
+      } else {
+        const __half2 bias = __float2half2_rn(1032.0f);  // 1024 + 8
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {  // 16-byte raw chunks = 32 nibbles = one scale block
+          const int c = (cc + dr) & 1;
+          const uint4 w = *reinterpret_cast<const uint4*>(raw + c * 16);
+          const __half2 sc2 = c == 0 ? s_lo : s_hi;
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+          uint32_t out[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lo = (wv[j] & 0x0F0F0F0Fu) ^ 0x08080808u;        // even elements
+            const uint32_t hi = ((wv[j] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;  // odd elements
+            const uint32_t e03 = __byte_perm(lo, hi, 0x5140);  // bytes e0 e1 e2 e3
+            const uint32_t e47 = __byte_perm(lo, hi, 0x7362);  // bytes e4 e5 e6 e7
+            uint32_t p0 = __byte_perm(e03, 0x64646464u, 0x4140);
+            uint32_t p1 = __byte_perm(e03, 0x64646464u, 0x4342);
+            uint32_t p2 = __byte_perm(e47, 0x64646464u, 0x4140);
+            uint32_t p3 = __byte_perm(e47, 0x64646464u, 0x4342);
+            __half2 h0 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&p0), bias), sc2);
+            __half2 h1 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&p1), bias), sc2);
+            __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&p2), bias), sc2);
+            __half2 h3 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&p3), bias), sc2);
+            out[4 * j] = *reinterpret_cast<uint32_t*>(&h0);
+            out[4 * j + 1] = *reinterpret_cast<uint32_t*>(&h1);
+            out[4 * j + 2] = *reinterpret_cast<uint32_t*>(&h2);
+            out[4 * j + 3] = *reinterpret_cast<uint32_t*>(&h3);
+          }
+#pragma unroll
+          for (int o = 0; o < 4; ++o) {
+            const int oc = 4 * c + o;
+            *reinterpret_cast<uint4*>(arow + ((oc ^ (dr & 7)) << 4)) =
+                make_uint4(out[4 * o], out[4 * o + 1], out[4 * o + 2], out[4 * o + 3]);
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to tcgen05.mma
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[as]);
+        mbar_arrive(&raw_empty[rs]);
+      }
+    }
   }
   __syncwarp();
 
@@ -251,8 +413,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       __syncthreads_and(mbar_wait(&done_bar, 0, p.err, ERR_TIMEOUT_DONE) ? 1 : 0) != 0 && nkt > 0;
   tc_fence_after();
   float acc[N], acc2[DUAL ? N : 1];
-  if (have) {
-    const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16);
+  const bool epi_warp = warp >= EPI0 && warp < EPI0 + 4;
+  if (have && epi_warp) {
+    const uint32_t taddr = tmem + (uint32_t((warp & 3) * 32) << 16);
     tmem_ld<N>(taddr, acc);
     if (DUAL) tmem_ld<N>(taddr + N, acc2);
   }
@@ -263,7 +426,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                  "r"(C::TMEM_COLS));
   }
   const bool ok = have && !abort_flag;  // CTA-uniform
-  const int r = warp * 32 + lane;        // row within the tile
+  const int r = (warp & 3) * 32 + lane;       // row within the tile (epilogue warps)
+  const int etid = (warp - EPI0) * 32 + lane;  // 0..127 on epilogue warps
   const int row = m0 + r;
 
   if (p.k_splits > 1) {
@@ -279,9 +443,9 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     const int rank = (int)cl.block_rank();
     const int own_rows = BM / ks;
     const int old_ = own_rows + 4;  // padded row stride of the receive buffer
-    float* red = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+    float* red = reinterpret_cast<float*>(smem + C::RING_BYTES);
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every peer has started
-    if (ok) {
+    if (ok && epi_warp) {
       const int sl = r / 16, owner = sl % ks;
       const int lr = (sl / ks) * 16 + (r % 16);
       float* dst = cl.map_shared_rank(red, owner);
@@ -297,10 +461,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     pdl_wait();
     pdl_launch_dependents();
     const int nv = own_rows * N;
-    if (!DUAL && ok && (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL)) {
+    if (!DUAL && ok && epi_warp && (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL)) {
 #pragma unroll
       for (int k = 0; k < MAXV; ++k) {
-        const int v = tid + k * THREADS;
+        const int v = etid + k * THREADS;
         yv[k] = 0.f;
         if (v < nv) {
           const int lr = v % own_rows, t = v / own_rows;
@@ -316,10 +480,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       }
     }
     cl.sync();  // every partial row has reached its owner
-    if (ok) {
+    if (ok && epi_warp) {
 #pragma unroll
       for (int k = 0; k < MAXV; ++k) {
-        const int v = tid + k * THREADS;
+        const int v = etid + k * THREADS;
         if (v >= nv) break;
         const int lr = v % own_rows, t = v / own_rows;
         const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
@@ -347,7 +511,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     return;
   }
 
-  if (!ok) return;
+  if (!ok || !epi_warp) return;
   pdl_wait();  // epilogue reads / writes buffers the previous kernel may touch
   pdl_launch_dependents();
 
@@ -465,6 +629,22 @@ int make_tmap_f16(CUtensorMap* m, const void* base, uint64_t rows, int cols, int
   return r == CUDA_SUCCESS ? B2D_OK : B2D_ERR_ALIGN;
 }
 
+// 2D uint8 tensor [rows, cols] (bytes), box {box_cols, box_rows}, no swizzle: the raw tiles of
+// quantized weights, which the dequant warps read with plain shared-memory loads.
+static int make_tmap_u8(CUtensorMap* m, const void* base, uint64_t rows, int cols, int box_cols,
+                        int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return B2D_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2D_OK : B2D_ERR_ALIGN;
+}
+
 constexpr int kMaxTiles = 4096;  // row tiles per call: M <= 4096 * 128
 
 struct TcPlan {
@@ -498,10 +678,10 @@ size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue) {
   return tc_plan(M, K, batch, epilogue).total;
 }
 
-template <int N, bool DUAL, bool ARGMAX>
+template <int N, bool DUAL, bool ARGMAX, int QUANT = 0>
 static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
-  using C = tc::Cfg<N, DUAL>;
-  auto kern = tc::tc_gemm_kernel<N, DUAL, ARGMAX>;
+  using C = tc::Cfg<N, DUAL, QUANT>;
+  auto kern = tc::tc_gemm_kernel<N, DUAL, ARGMAX, QUANT>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -515,7 +695,7 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(tc::THREADS);
+  cfg.blockDim = dim3(tc::threads_for(QUANT));
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -543,10 +723,10 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
 // K splits (= cluster size) for a row-tile count: the largest power of two <= 8 whose clusters
 // all fit on the GPU in one wave (cudaOccupancyMaxActiveClusters for this kernel), without
 // more CTAs than SMs and without splitting K below one 64-wide tile.
-template <int N, bool DUAL>
+template <int N, bool DUAL, int QUANT = 0>
 static int tc_pick_splits(int m_tiles, int k_tiles) {
-  using C = tc::Cfg<N, DUAL>;
-  auto kern = tc::tc_gemm_kernel<N, DUAL, false>;
+  using C = tc::Cfg<N, DUAL, QUANT>;
+  auto kern = tc::tc_gemm_kernel<N, DUAL, false, QUANT>;
   static int cached_dev = -1;
   static int max_clusters[4] = {0, 0, 0, 0};  // cluster sizes 1, 2, 4, 8
   int dev = 0;
@@ -556,7 +736,7 @@ static int tc_pick_splits(int m_tiles, int k_tiles) {
     for (int i = 0; i < 4; ++i) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, 1 << i);
-      cfg.blockDim = dim3(tc::THREADS);
+      cfg.blockDim = dim3(tc::threads_for(QUANT));
       cfg.dynamicSmemBytes = C::SMEM;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -588,6 +768,7 @@ struct TcCall {
   dim3 grid;
   int n_tile;
   bool dual, argmax;
+  int quant = 0;  // 0 fp16, 1 q8_32, 2 q4_32
 };
 
 int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
@@ -649,6 +830,12 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
 }
 
 int tc_gemm_launch(const TcCall& c, cudaStream_t stream) {
+  if (c.quant == 1)
+    return c.n_tile == 16 ? launch_tc<16, false, false, 1>(c.prm, c.grid, stream)
+                          : launch_tc<32, false, false, 1>(c.prm, c.grid, stream);
+  if (c.quant == 2)
+    return c.n_tile == 16 ? launch_tc<16, false, false, 2>(c.prm, c.grid, stream)
+                          : launch_tc<32, false, false, 2>(c.prm, c.grid, stream);
   if (c.n_tile == 16) {
     if (c.argmax) return launch_tc<16, false, true>(c.prm, c.grid, stream);
     if (c.dual) return launch_tc<16, true, false>(c.prm, c.grid, stream);
@@ -666,6 +853,58 @@ int tc_gemm(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
   TcCall c;
   B2D_TRY(tc_gemm_prepare(&c, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
                           logits, tokens, max_vals, index_offset, workspace, workspace_bytes));
+  return tc_gemm_launch(c, stream);
+}
+
+// Quantized weights (q8_32 / q4_32) on the tensor cores: STORE / ADD / GELU_MUL epilogues.
+int tc_gemm_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X, int ldx,
+              int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
+              int batch, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!q || !scales || !X || !y) return B2D_ERR_NULL;
+  if (w_dtype != B2D_Q8_32 && w_dtype != B2D_Q4_32) return B2D_ERR_UNSUPPORTED;
+  if (epilogue != B2D_EPI_STORE && epilogue != B2D_EPI_ADD && epilogue != B2D_EPI_GELU_MUL)
+    return B2D_ERR_UNSUPPORTED;
+  if (y_dtype != B2D_F32 && y_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
+  if (epilogue == B2D_EPI_GELU_MUL && !aux) return B2D_ERR_NULL;
+  if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 32 || ldx < K || ldx % 8 || ldy < M ||
+      M > kMaxTiles * tc::BM)
+    return B2D_ERR_SHAPE;
+  if (!aligned16(q) || !aligned16(X) || (reinterpret_cast<uintptr_t>(scales) & 1))
+    return B2D_ERR_ALIGN;
+  const TcPlan pl = tc_plan(M, K, batch, epilogue);
+  if (!workspace || workspace_bytes < pl.total) return B2D_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return B2D_ERR_ALIGN;
+  const int quant = w_dtype == B2D_Q8_32 ? 1 : 2;
+  TcCall c;
+  tc::Params& p = c.prm;
+  p = tc::Params{};
+  const int row_bytes = quant == 1 ? K : K / 2;
+  B2D_TRY(make_tmap_u8(&p.tmA, q, M, row_bytes, quant == 1 ? tc::BK : tc::BK / 2, tc::BM));
+  B2D_TRY(make_tmap_f16(&p.tmB, X, batch, K, ldx, pl.n_tile));
+  char* ws = static_cast<char*>(workspace);
+  p.M = M;
+  p.K = K;
+  p.batch = batch;
+  p.k_tiles = pl.k_tiles;
+  p.m_tiles = pl.m_tiles;
+  p.epi = epilogue;
+  p.y = y;
+  p.y_f16 = y_dtype == B2D_F16;
+  p.ldy = ldy;
+  p.aux = aux;
+  p.err = reinterpret_cast<int*>(ws);
+  p.am_counter = reinterpret_cast<unsigned int*>(ws + 64);
+  p.scales = scales;
+  p.k_splits = pl.n_tile == 16
+                   ? (quant == 1 ? tc_pick_splits<16, false, 1>(pl.m_tiles, pl.k_tiles)
+                                 : tc_pick_splits<16, false, 2>(pl.m_tiles, pl.k_tiles))
+                   : (quant == 1 ? tc_pick_splits<32, false, 1>(pl.m_tiles, pl.k_tiles)
+                                 : tc_pick_splits<32, false, 2>(pl.m_tiles, pl.k_tiles));
+  c.grid = dim3(pl.m_tiles, p.k_splits);
+  c.n_tile = pl.n_tile;
+  c.dual = false;
+  c.argmax = false;
+  c.quant = quant;
   return tc_gemm_launch(c, stream);
 }
 

@@ -413,6 +413,55 @@ def gemm_tc(
     return y
 
 
+def gemm_tc_q(
+    Wq: QWeight,
+    X: torch.Tensor,
+    *,
+    epilogue: str = "store",
+    aux: torch.Tensor | None = None,
+    y: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.float32,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Tensor-core batched GEMV over 32-block quantized weights: y[b] = epilogue(W @ X[b]) with
+    W = scale * q dequantized in shared memory to fp16 (the MMA operand), fp16 X [batch <= 32, K].
+    Epilogues 'store', 'add', 'gelu_mul'."""
+    M, K = Wq.shape
+    B = X.shape[0]
+    if X.dtype != torch.float16 or X.shape[1] != K:
+        raise ValueError("gemm_tc_q needs fp16 X [batch, K]")
+    if epilogue not in ("store", "add", "gelu_mul"):
+        raise ValueError(f"gemm_tc_q: unsupported epilogue {epilogue!r}")
+    ws = workspace if workspace is not None else _WS_TC.get(tc_workspace_bytes(M, K, B, epilogue), X.device)
+    if y is None:
+        if epilogue == "add":
+            raise ValueError("epilogue 'add' needs y")
+        y = torch.empty(B, M, dtype=out_dtype, device=X.device)
+    if y.dtype not in _DT or tuple(y.shape) != (B, M):
+        raise ValueError(f"y must be fp32/fp16 [{B}, {M}]")
+    _need_cuda(Wq.q, Wq.scales, X, aux, y, ws)
+    call(
+        "b2d_gemm_tc_q",
+        Wq.dtype_code,
+        Wq.q.data_ptr(),
+        Wq.scales.data_ptr(),
+        X.data_ptr(),
+        K,
+        _TC_EPI[epilogue],
+        _DT[y.dtype],
+        y.data_ptr(),
+        M,
+        _ptr(aux),
+        M,
+        K,
+        B,
+        ws.data_ptr(),
+        ws.numel(),
+        _stream(),
+    )
+    return y
+
+
 def add_rmsnorm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float, p: torch.Tensor | None = None) -> torch.Tensor:
     """x += p (if given, in place); returns fp16 rmsnorm(x) * gamma."""
     out = torch.empty(x.shape, dtype=torch.float16, device=x.device)

@@ -148,6 +148,18 @@ B2D_API int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t*
                         int batch, float* logits, int* tokens, float* max_vals, int index_offset,
                         void* workspace, size_t workspace_bytes, b2d_stream_t stream);
 
+/* The tensor-core batched GEMV for 32-block quantized weights (w_dtype B2D_Q8_32 or B2D_Q4_32,
+ * layouts above; scales fp16 [M, K/32]): TMA streams the raw weight tiles through a deep
+ * shared-memory ring and dequantizer warps expand them to fp16(scale * q) -- the MMA operand --
+ * so the batch reads every weight byte once.  X fp16 [batch <= 32, K], K a multiple of 32;
+ * epilogues STORE / ADD / GELU_MUL into y (fp32 or fp16, row stride ldy).  Workspace as
+ * b2d_gemm_tc_workspace_bytes(M, K, batch, epilogue).  (Extension: the reference has no
+ * quantized weights, ios_kernels/PLAN.md:175,256.) */
+B2D_API int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X,
+                          int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux,
+                          int M, int K, int batch, void* workspace, size_t workspace_bytes,
+                          b2d_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------
  * Small ops of the decode step
  * ------------------------------------------------------------------------------------- */

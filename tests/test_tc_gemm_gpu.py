@@ -10,7 +10,7 @@ import torch
 
 from gemmagemini4hackathon2026_10_2425_b200 import ops
 from oracle import ops as O
-from tests._tol import assert_rel_close
+from tests._tol import assert_norm_close, assert_rel_close
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -114,3 +114,57 @@ def test_tc_workspace_shared_across_shapes():
         W, X = case(M, K, 32, M * 3 + K)
         y = ops.gemm_tc(d(W), d(X), workspace=ws).cpu().numpy()
         assert_rel_close(y, O.gemv(W, X), 2e-3, what=f"shared ws {M}x{K}")
+
+
+def qcase(M, K, fmt, seed):
+    r = np.random.default_rng(seed)
+    sc = np.abs(r.standard_normal((M, K // 32)) * 0.01).astype(np.float16)
+    if fmt == "q8":
+        q = r.integers(-127, 128, size=(M, K), dtype=np.int8)
+        return q, q, sc
+    qv = r.integers(-8, 8, size=(M, K), dtype=np.int8)
+    return qv, O.pack_q4(qv), sc
+
+
+# The quantized tensor-core operand is fp16(scale * q): one fp16 rounding per weight, so the
+# check is max-normalized (2e-3 of max|y|), not elementwise.
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+@pytest.mark.parametrize("M,K", [(4096, 4096), (14336, 4096), (4096, 14336), (96, 64), (200, 96), (1000, 544)])
+@pytest.mark.parametrize("b", [9, 16, 32])
+def test_tc_quant_config3(fmt, M, K, b):
+    qv, packed, sc = qcase(M, K, fmt, M + 7 * K + b)
+    X = np.random.default_rng(b).standard_normal((b, K)).astype(np.float16)
+    Wq = ops.QWeight(fmt, d(packed), d(sc))
+    y = ops.gemm_tc_q(Wq, d(X)).cpu().numpy()
+    assert_norm_close(y, O.gemv(O.dequant_q8_32(qv, sc), X), 2e-3, what=f"tc {fmt} {M}x{K} b{b}")
+
+
+@pytest.mark.parametrize("fmt", ["q8", "q4"])
+def test_tc_quant_add_gelu_fp16_out(fmt):
+    M, K, b = 2048, 8192, 16
+    qv, packed, sc = qcase(M, K, fmt, 31)
+    W = O.dequant_q8_32(qv, sc)
+    r = np.random.default_rng(32)
+    X = r.standard_normal((b, K)).astype(np.float16)
+    y0 = r.standard_normal((b, M)).astype(np.float32)
+    aux = r.standard_normal((b, M)).astype(np.float32)
+    Wq = ops.QWeight(fmt, d(packed), d(sc))
+    y = d(y0.copy())
+    ops.gemm_tc_q(Wq, d(X), epilogue="add", y=y)
+    y2 = d(y0.copy())
+    ops.gemm_tc_q(Wq, d(X), epilogue="add", y=y2)
+    np.testing.assert_array_equal(y.cpu().numpy(), y2.cpu().numpy())  # deterministic split-K
+    assert_norm_close(y.cpu().numpy(), y0 + O.gemv(W, X), 2e-3, what=f"{fmt} add")
+    g = ops.gemm_tc_q(Wq, d(X), epilogue="gelu_mul", aux=d(aux), out_dtype=torch.float16)
+    ref = O.gemv_fused(W, X.astype(np.float32), None, 0.0, O.EPI_GELU_MUL, aux=aux)
+    assert_norm_close(g.float().cpu().numpy(), ref, 3e-3, what=f"{fmt} gelu_mul")
+
+
+def test_tc_quant_bad_arguments_raise():
+    qv, packed, sc = qcase(256, 96, "q8", 3)
+    Wq = ops.QWeight("q8", d(packed), d(sc))
+    with pytest.raises(ValueError):
+        ops.gemm_tc_q(Wq, d(np.zeros((33, 96), np.float16)))  # batch > 32
+    with pytest.raises(ValueError):
+        ops.gemm_tc_q(Wq, d(np.zeros((4, 96), np.float16)), epilogue="swiglu")
+
