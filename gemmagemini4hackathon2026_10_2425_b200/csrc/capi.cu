@@ -49,6 +49,11 @@ int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, vo
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
 int tc_gemm_q(int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
               const float*, int, int, int, void*, size_t, cudaStream_t);
+int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
+                             float*, const float*, float, uint16_t*, int, int, long long, int*,
+                             cudaStream_t);
+int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, uint32_t*, int,
+                     int, int, int, int*, long long, int*, cudaStream_t);
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
@@ -187,6 +192,21 @@ int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint
                   int batch, void* workspace, size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm_q(w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
                    workspace, workspace_bytes, S(stream));
+}
+
+int b2d_tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs,
+                                 uint32_t* epochs, int rank, int tp, int slot0, float* x,
+                                 const float* gamma, float eps, uint16_t* out16, int D, int rows,
+                                 long long timeout_ns, int* err, b2d_stream_t stream) {
+  return tp_allreduce_add_rmsnorm(parts, sigs, epochs, rank, tp, slot0, x, gamma, eps, out16, D,
+                                  rows, timeout_ns, err, S(stream));
+}
+
+int b2d_tp_argmax_gather(const float* const* vals, const int* const* idxs, uint32_t* const* sigs,
+                         uint32_t* epochs, int rank, int tp, int slot, int B, int* tokens,
+                         long long timeout_ns, int* err, b2d_stream_t stream) {
+  return tp_argmax_gather(vals, idxs, sigs, epochs, rank, tp, slot, B, tokens, timeout_ns, err,
+                          S(stream));
 }
 
 int b2d_inv_freq(int head_dim, double theta, float* out_host) {

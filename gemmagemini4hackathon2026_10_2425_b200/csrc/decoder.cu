@@ -13,13 +13,17 @@
 //
 // Tensor parallelism (tp > 1, one process per GPU): QKV and gate/up are column-parallel (this
 // rank's heads / FFN rows), O and down are row-parallel and their partial sums are summed
-// with ncclAllReduce before the residual add; the LM head is vocab-parallel and each rank's
-// (max, index) pair is all-gathered and combined (ties -> lowest index).  The whole step can
-// be captured once into a CUDA graph and replayed.
+// before the residual add; the LM head is vocab-parallel and each rank's (max, index) pair is
+// gathered and combined (ties -> lowest index).  The sums and the gather run over NVLink peer
+// memory (tp_peer.cu: one kernel = all-reduce + residual add + next RMSNorm), with NCCL
+// (ncclAllReduce / ncclAllGather) as the path where the ranks cannot map each other's memory
+// or B2D_TP_COLLECTIVE=nccl asks for it.  The whole step can be captured once into a CUDA
+// graph and replayed.
 #include <nccl.h>
 
 #include <cmath>
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -45,10 +49,18 @@ int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, 
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
+int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
+                             float*, const float*, float, uint16_t*, int, int, long long, int*,
+                             cudaStream_t);
+int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, uint32_t*, int,
+                     int, int, int, int*, long long, int*, cudaStream_t);
 }  // namespace b2d
 
 // Batches of at least this many sequences run their projections on the tensor cores.
 static constexpr int kTcMinBatch = 9;
+static constexpr int kMaxTp = 8;
+// Bound on a peer-barrier wait (a rank that never arrives turns into B2D_ERR_TIMEOUT).
+static constexpr long long kPeerTimeoutNs = 10000000000LL;
 
 using namespace b2d;
 
@@ -91,12 +103,9 @@ struct b2d_decoder {
   float* qkv = nullptr;     // [B, qkv_l]
   float* att = nullptr;     // [B, hq*HD]
   float* hid = nullptr;     // [B, fl]
-  float* part = nullptr;    // [B, D] row-parallel partial (tp > 1)
   float* invf = nullptr;    // [HD/2]
   float* cand_val = nullptr;  // [tp, B]
   int* cand_idx = nullptr;    // [tp, B]
-  float* my_val = nullptr;    // [B]
-  int* my_idx = nullptr;      // [B]
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   void* am_ws = nullptr;
@@ -107,6 +116,16 @@ struct b2d_decoder {
   uint16_t* h16 = nullptr;    // [B, fl]
   void* tc_ws = nullptr;
   size_t tc_ws_bytes = 0;
+  // tensor parallelism: buffers the peers read (one IPC-shared allocation per rank)
+  bool peer = false;                   // peer-memory collectives (else NCCL)
+  void* peer_arena = nullptr;          // this rank's shared buffers
+  void* peer_open[kMaxTp] = {};        // peers' arenas mapped here (nullptr for this rank)
+  float* parts[2][kMaxTp] = {};        // row-parallel partials [B, D], two alternating buffers
+  float* am_val[kMaxTp] = {};          // LM-head (max, index) per token [B]
+  int* am_idx[kMaxTp] = {};
+  uint32_t* sigs[kMaxTp] = {};         // signal arrays [(B + 1) slots][kMaxTp]
+  uint32_t* epochs = nullptr;          // this rank's barrier epochs [(B + 1) slots]
+  int* err = nullptr;                  // device error word of the peer kernels
   // graph cache
   cudaGraphExec_t gexec = nullptr;
   GraphKey gkey;
@@ -121,6 +140,32 @@ static int cuda_status(cudaError_t e) {
 }
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// Sum the ranks' row-parallel partials (buffer `buf`) into the residual x; with gamma, also
+// write fp16(rmsnorm(x) * gamma) to out16.
+static int tp_reduce(b2d_decoder* h, int buf, const float* gamma, uint16_t* out16, int B,
+                     cudaStream_t s) {
+  const int D = h->cfg.dim;
+  if (h->peer)
+    return tp_allreduce_add_rmsnorm(h->parts[buf], h->sigs, h->epochs, h->rank, h->tp, 0, h->x,
+                                    gamma, h->cfg.eps, out16, D, B, kPeerTimeoutNs, h->err, s);
+  float* mine = h->parts[buf][h->rank];
+  B2D_TRY(nccl_status(ncclAllReduce(mine, mine, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
+  return gamma ? add_rmsnorm_f16(h->x, mine, gamma, h->cfg.eps, out16, B, D, s)
+               : add_f32(h->x, mine, (size_t)B * D, s);
+}
+
+// Combine the ranks' LM-head (max, index) pairs into next_tokens.
+static int tp_argmax(b2d_decoder* h, int B, int* next_tokens, cudaStream_t s) {
+  if (h->peer)
+    return tp_argmax_gather(h->am_val, h->am_idx, h->sigs, h->epochs, h->rank, h->tp,
+                            h->cfg.max_batch, B, next_tokens, kPeerTimeoutNs, h->err, s);
+  B2D_TRY(nccl_status(ncclGroupStart()));
+  B2D_TRY(nccl_status(ncclAllGather(h->am_val[h->rank], h->cand_val, B, ncclFloat, h->comm, s)));
+  B2D_TRY(nccl_status(ncclAllGather(h->am_idx[h->rank], h->cand_idx, B, ncclInt32, h->comm, s)));
+  B2D_TRY(nccl_status(ncclGroupEnd()));
+  return argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s);
+}
 
 // Tensor-core step (batch >= kTcMinBatch): activations enter each projection as fp16
 // (RMSNorm fused into the producer of the operand), weights are read once per step.
@@ -151,11 +196,9 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                       HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, B, D, s));
     } else {
-      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_STORE, B2D_F32, h->part, D, nullptr,
-                      D, HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-      B2D_TRY(nccl_status(
-          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
-      B2D_TRY(add_rmsnorm_f16(h->x, h->part, L.ffn_norm, c.eps, h->xn16, B, D, s));
+      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_STORE, B2D_F32, h->parts[0][h->rank],
+                      D, nullptr, D, HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+      B2D_TRY(tp_reduce(h, 0, L.ffn_norm, h->xn16, B, s));
     }
     // gate/up SwiGLU (column-parallel) -> fp16
     B2D_TRY(tc_gemm(L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, B2D_F16, h->h16, h->fl, nullptr,
@@ -166,11 +209,10 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                       h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, B, D, s));
     } else {
-      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_STORE, B2D_F32, h->part, D,
-                      nullptr, D, h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-      B2D_TRY(nccl_status(
-          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
-      B2D_TRY(add_rmsnorm_f16(h->x, h->part, next_norm, c.eps, h->xn16, B, D, s));
+      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_STORE, B2D_F32,
+                      h->parts[1][h->rank], D, nullptr, D, h->fl, B, nullptr, nullptr, nullptr, 0,
+                      ws, wsb, s));
+      B2D_TRY(tp_reduce(h, 1, next_norm, h->xn16, B, s));
     }
   }
   // LM head (vocab-parallel) + argmax
@@ -180,12 +222,9 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                     h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s));
   } else {
     B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
-                    h->lm_rows, D, B, logits, h->my_idx, h->my_val, offset, ws, wsb, s));
-    B2D_TRY(nccl_status(ncclGroupStart()));
-    B2D_TRY(nccl_status(ncclAllGather(h->my_val, h->cand_val, B, ncclFloat, h->comm, s)));
-    B2D_TRY(nccl_status(ncclAllGather(h->my_idx, h->cand_idx, B, ncclInt32, h->comm, s)));
-    B2D_TRY(nccl_status(ncclGroupEnd()));
-    B2D_TRY(argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s));
+                    h->lm_rows, D, B, logits, h->am_idx[h->rank], h->am_val[h->rank], offset, ws,
+                    wsb, s));
+    B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
   return B2D_OK;
 }
@@ -218,11 +257,9 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                             h->hq * HD, B, s));
     } else {
       B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
-                            h->hq * HD, nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->part, D,
-                            nullptr, D, h->hq * HD, B, s));
-      B2D_TRY(nccl_status(
-          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
-      B2D_TRY(add_f32(h->x, h->part, (size_t)B * D, s));
+                            h->hq * HD, nullptr, 0.f, B2D_EPI_STORE, B2D_F32,
+                            h->parts[0][h->rank], D, nullptr, D, h->hq * HD, B, s));
+      B2D_TRY(tp_reduce(h, 0, nullptr, nullptr, B, s));
     }
     // RMSNorm + gate/up SwiGLU (column-parallel: this rank's FFN rows)
     B2D_TRY(gemv_dispatch(B2D_F16, L.wgate, nullptr, L.wup, nullptr, B2D_F32, h->x, D,
@@ -235,11 +272,9 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                             s));
     } else {
       B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
-                            nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->part, D, nullptr, D, h->fl,
-                            B, s));
-      B2D_TRY(nccl_status(
-          ncclAllReduce(h->part, h->part, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
-      B2D_TRY(add_f32(h->x, h->part, (size_t)B * D, s));
+                            nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->parts[1][h->rank], D,
+                            nullptr, D, h->fl, B, s));
+      B2D_TRY(tp_reduce(h, 1, nullptr, nullptr, B, s));
     }
   }
   // final RMSNorm + LM head (vocab-parallel) + argmax
@@ -249,13 +284,81 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                            logits, next_tokens, nullptr, h->am_ws, h->am_ws_bytes, s));
   } else {
     B2D_TRY(lm_head_argmax(h->lm_head, h->x, D, h->final_norm, c.eps, h->lm_rows, D, B, offset,
-                           logits, h->my_idx, h->my_val, h->am_ws, h->am_ws_bytes, s));
-    B2D_TRY(nccl_status(ncclGroupStart()));
-    B2D_TRY(nccl_status(ncclAllGather(h->my_val, h->cand_val, B, ncclFloat, h->comm, s)));
-    B2D_TRY(nccl_status(ncclAllGather(h->my_idx, h->cand_idx, B, ncclInt32, h->comm, s)));
-    B2D_TRY(nccl_status(ncclGroupEnd()));
-    B2D_TRY(argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s));
+                           logits, h->am_idx[h->rank], h->am_val[h->rank], h->am_ws,
+                           h->am_ws_bytes, s));
+    B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
+  return B2D_OK;
+}
+
+// Tensor-parallel buffers that the peers read: partials (2 x [B, D] fp32), LM-head (max, index)
+// [B] and the signal array.  With CUDA IPC every rank maps every peer's allocation (handles are
+// exchanged with one ncclAllGather); if any rank cannot, or B2D_TP_COLLECTIVE=nccl, all ranks
+// keep their buffers local and use NCCL collectives instead (decided together: ncclMin).
+static int setup_peers(b2d_decoder* h) {
+  const int B = h->cfg.max_batch, D = h->cfg.dim, tp = h->tp;
+  const size_t part_b = align256((size_t)B * D * 4), am_b = align256((size_t)B * 4);
+  const size_t sig_b = align256((size_t)(B + 1) * kMaxTp * 4);
+  const size_t total = 2 * part_b + 2 * am_b + sig_b;
+  B2D_TRY(cuda_status(cudaMalloc(&h->peer_arena, total)));
+  B2D_TRY(cuda_status(cudaMemset(h->peer_arena, 0, total)));
+  B2D_TRY(cuda_status(cudaDeviceSynchronize()));  // signals are zero before any peer can write
+  char* base[kMaxTp] = {};
+  base[h->rank] = static_cast<char*>(h->peer_arena);
+  const char* env = std::getenv("B2D_TP_COLLECTIVE");
+  int ok = !(env && std::strcmp(env, "nccl") == 0);
+  cudaIpcMemHandle_t mine;
+  if (ok && cudaIpcGetMemHandle(&mine, h->peer_arena) != cudaSuccess) ok = 0;
+  cudaGetLastError();
+  // exchange the handles (and whether this rank can take part) over the communicator
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  std::vector<char> all(hb * tp, 0);
+  char* dev = nullptr;
+  B2D_TRY(cuda_status(cudaMalloc(&dev, hb * tp + 16)));
+  int* dok = reinterpret_cast<int*>(dev + hb * tp);
+  int st = B2D_OK;
+  if (ok) cudaMemcpy(dev + hb * h->rank, &mine, hb, cudaMemcpyHostToDevice);
+  if (ncclAllGather(dev + hb * h->rank, dev, hb, ncclChar, h->comm, nullptr) != ncclSuccess)
+    st = B2D_ERR_NCCL;
+  if (st == B2D_OK) st = cuda_status(cudaMemcpy(all.data(), dev, hb * tp, cudaMemcpyDeviceToHost));
+  for (int r = 0; st == B2D_OK && ok && r < tp; ++r) {
+    if (r == h->rank) continue;
+    cudaIpcMemHandle_t hr;
+    memcpy(&hr, all.data() + hb * r, hb);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    }
+    h->peer_open[r] = p;
+    base[r] = static_cast<char*>(p);
+  }
+  if (st == B2D_OK) {
+    cudaMemcpy(dok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+    if (ncclAllReduce(dok, dok, 1, ncclInt32, ncclMin, h->comm, nullptr) != ncclSuccess)
+      st = B2D_ERR_NCCL;
+    else
+      st = cuda_status(cudaMemcpy(&ok, dok, sizeof(int), cudaMemcpyDeviceToHost));
+  }
+  cudaFree(dev);
+  B2D_TRY(st);
+  h->peer = ok != 0;
+  for (int r = 0; r < tp; ++r) {
+    char* b = h->peer ? base[r] : (r == h->rank ? base[r] : nullptr);
+    if (!b) continue;
+    h->parts[0][r] = reinterpret_cast<float*>(b);
+    h->parts[1][r] = reinterpret_cast<float*>(b + part_b);
+    h->am_val[r] = reinterpret_cast<float*>(b + 2 * part_b);
+    h->am_idx[r] = reinterpret_cast<int*>(b + 2 * part_b + am_b);
+    h->sigs[r] = reinterpret_cast<uint32_t*>(b + 2 * part_b + 2 * am_b);
+  }
+  if (!h->peer)
+    for (int r = 0; r < kMaxTp; ++r)
+      if (h->peer_open[r]) {
+        cudaIpcCloseMemHandle(h->peer_open[r]);
+        h->peer_open[r] = nullptr;
+      }
   return B2D_OK;
 }
 
@@ -322,9 +425,9 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   }
   size_t sizes[] = {
       (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,
-      (size_t)B * h->fl * 4,      (size_t)B * D * 4,        (size_t)c.head_dim / 2 * 4,
-      (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)B * 4,
-      (size_t)B * 4,              h->attn_ws_bytes,         h->am_ws_bytes,
+      (size_t)B * h->fl * 4,      (size_t)(B + 1) * 4,      (size_t)c.head_dim / 2 * 4,
+      (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)4,
+      h->attn_ws_bytes,           h->am_ws_bytes,
       (size_t)B * D * 2,          (size_t)B * h->hq * c.head_dim * 2, (size_t)B * h->fl * 2,
       h->tc_ws_bytes};
   size_t total = 0;
@@ -337,9 +440,9 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   cudaMemset(h->arena, 0, total);
   char* p = static_cast<char*>(h->arena);
   void** slots[] = {(void**)&h->x,        (void**)&h->qkv,      (void**)&h->att,
-                    (void**)&h->hid,      (void**)&h->part,     (void**)&h->invf,
-                    (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->my_val,
-                    (void**)&h->my_idx,   (void**)&h->attn_ws,  (void**)&h->am_ws,
+                    (void**)&h->hid,      (void**)&h->epochs,   (void**)&h->invf,
+                    (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->err,
+                    (void**)&h->attn_ws,  (void**)&h->am_ws,
                     (void**)&h->xn16,     (void**)&h->att16,    (void**)&h->h16,
                     (void**)&h->tc_ws};
   static_assert(sizeof(slots) / sizeof(slots[0]) == sizeof(sizes) / sizeof(sizes[0]),
@@ -353,13 +456,15 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
     invf[i] = (float)(1.0 / std::pow(c.rope_theta, (double)(2 * i) / (double)c.head_dim));
   st = cuda_status(cudaMemcpy(h->invf, invf.data(), invf.size() * 4, cudaMemcpyHostToDevice));
   if (st == B2D_OK && tp_size > 1) {
+    if (tp_size > kMaxTp) st = B2D_ERR_SHAPE;
     ncclUniqueId id;
     memcpy(&id, nccl_id, sizeof(id));
-    if (ncclCommInitRank(&h->comm, tp_size, id, tp_rank) != ncclSuccess) st = B2D_ERR_NCCL;
+    if (st == B2D_OK && ncclCommInitRank(&h->comm, tp_size, id, tp_rank) != ncclSuccess)
+      st = B2D_ERR_NCCL;
+    if (st == B2D_OK) st = setup_peers(h);
   }
   if (st != B2D_OK) {
-    cudaFree(h->arena);
-    delete h;
+    b2d_decoder_destroy(h);
     return st;
   }
   *out = h;
@@ -369,10 +474,29 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
 int b2d_decoder_destroy(b2d_decoder* h) {
   if (!h) return B2D_OK;
   if (h->gexec) cudaGraphExecDestroy(h->gexec);
+  if (h->comm && h->peer) {
+    // every rank stops reading its peers' buffers before any rank frees its own
+    cudaDeviceSynchronize();
+    ncclAllReduce(h->err, h->err, 1, ncclInt32, ncclMax, h->comm, nullptr);
+    cudaDeviceSynchronize();
+  }
+  for (int r = 0; r < kMaxTp; ++r)
+    if (h->peer_open[r]) cudaIpcCloseMemHandle(h->peer_open[r]);
   if (h->comm) ncclCommDestroy(h->comm);
+  if (h->peer_arena) cudaFree(h->peer_arena);
   if (h->arena) cudaFree(h->arena);
   delete h;
   return B2D_OK;
+}
+
+int b2d_decoder_peer_collectives(const b2d_decoder* h) { return h && h->peer ? 1 : 0; }
+
+int b2d_decoder_error(b2d_decoder* h) {
+  if (!h) return B2D_ERR_NULL;
+  int v = 0;
+  B2D_TRY(cuda_status(cudaMemcpy(&v, h->err, sizeof(int), cudaMemcpyDeviceToHost)));
+  if (v) B2D_TRY(cuda_status(cudaMemset(h->err, 0, sizeof(int))));
+  return v;
 }
 
 int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,

@@ -218,14 +218,27 @@ class DecodeEngine:
         )
         return next_tokens
 
+    def peer_collectives(self) -> bool:
+        """True if the tensor-parallel sums run over NVLink peer memory (False: NCCL or tp 1)."""
+        return bool(_lib.lib().b2d_decoder_peer_collectives(self._h))
+
+    def check(self) -> None:
+        """Synchronize and raise if a device-side peer barrier timed out since the last check."""
+        st = _lib.lib().b2d_decoder_error(self._h)
+        if st:
+            raise _lib.B2DError("b2d_decoder_error", st, _lib.lib().b2d_status_string(st).decode())
+
     def close(self) -> None:
+        """Free the handle.  With tp > 1 this is collective: every rank calls it."""
         if self._h:
             _lib.lib().b2d_decoder_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):  # pragma: no cover
+        # tensor-parallel handles are freed collectively by close(), never by the collector
         try:
-            self.close()
+            if self.tp == 1:
+                self.close()
         except Exception:
             pass
 

@@ -462,6 +462,85 @@ def gemm_tc_q(
     return y
 
 
+def _ptr_array(ts) -> ctypes.Array:
+    return (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+
+
+def tp_allreduce_add_rmsnorm(
+    parts: list[torch.Tensor],
+    sigs: list[torch.Tensor],
+    epochs: torch.Tensor,
+    rank: int,
+    x: torch.Tensor,
+    err: torch.Tensor,
+    gamma: torch.Tensor | None = None,
+    eps: float = 1e-5,
+    out16: torch.Tensor | None = None,
+    slot0: int = 0,
+    timeout_ns: int = 10_000_000_000,
+) -> torch.Tensor | None:
+    """x += parts[0] + ... + parts[tp-1] (rank order) after a per-row barrier on the ranks'
+    signal arrays; returns fp16 rmsnorm(x) * gamma if gamma is given.  parts: the ranks'
+    partials [rows, D] fp32 as mapped in this process; sigs: the ranks' uint32 signal arrays;
+    epochs: this rank's uint32 epoch counters; err: device int32 error word (a barrier that
+    times out writes B2D_ERR_TIMEOUT there and leaves its row unchanged)."""
+    rows, D = x.shape
+    if gamma is not None and out16 is None:
+        out16 = torch.empty(rows, D, dtype=torch.float16, device=x.device)
+    _need_cuda(x, err, epochs, gamma, out16, *parts, *sigs)
+    call(
+        "b2d_tp_allreduce_add_rmsnorm",
+        ctypes.cast(_ptr_array(parts), ctypes.c_void_p),
+        ctypes.cast(_ptr_array(sigs), ctypes.c_void_p),
+        epochs.data_ptr(),
+        rank,
+        len(parts),
+        slot0,
+        x.data_ptr(),
+        _ptr(gamma),
+        float(eps),
+        _ptr(out16),
+        D,
+        rows,
+        int(timeout_ns),
+        err.data_ptr(),
+        _stream(),
+    )
+    return out16
+
+
+def tp_argmax_gather(
+    vals: list[torch.Tensor],
+    idxs: list[torch.Tensor],
+    sigs: list[torch.Tensor],
+    epochs: torch.Tensor,
+    rank: int,
+    slot: int,
+    err: torch.Tensor,
+    timeout_ns: int = 10_000_000_000,
+) -> torch.Tensor:
+    """Best (value, index) over the ranks' LM-head candidates per token (ties -> lower index)."""
+    B = vals[0].numel()
+    tokens = torch.empty(B, dtype=torch.int32, device=vals[0].device)
+    _need_cuda(tokens, epochs, err, *vals, *idxs, *sigs)
+    call(
+        "b2d_tp_argmax_gather",
+        ctypes.cast(_ptr_array(vals), ctypes.c_void_p),
+        ctypes.cast(_ptr_array(idxs), ctypes.c_void_p),
+        ctypes.cast(_ptr_array(sigs), ctypes.c_void_p),
+        epochs.data_ptr(),
+        rank,
+        len(vals),
+        slot,
+        B,
+        tokens.data_ptr(),
+        int(timeout_ns),
+        err.data_ptr(),
+        _stream(),
+    )
+    return tokens
+
+
 def add_rmsnorm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float, p: torch.Tensor | None = None) -> torch.Tensor:
     """x += p (if given, in place); returns fp16 rmsnorm(x) * gamma."""
     out = torch.empty(x.shape, dtype=torch.float16, device=x.device)

@@ -280,12 +280,22 @@ typedef struct {
 B2D_API int b2d_nccl_unique_id_bytes(void);
 B2D_API int b2d_nccl_get_unique_id(void* out_host);
 
-/* Create a decoder for rank `tp_rank` of `tp_size` on the current CUDA device.  With
- * tp_size > 1, nccl_id (host, 128 bytes from rank 0) sets up the communicator.  The handle
- * allocates its activation buffers once; weights and KV pages stay owned by the caller. */
+/* Create a decoder for rank `tp_rank` of `tp_size` (<= 8) on the current CUDA device.  With
+ * tp_size > 1, nccl_id (host, 128 bytes from rank 0) sets up the communicator, and the ranks
+ * map each other's partial-sum buffers (CUDA IPC) so the row-parallel sums and the LM-head
+ * gather run over NVLink peer memory; where any rank cannot map them, or the environment sets
+ * B2D_TP_COLLECTIVE=nccl, all ranks use ncclAllReduce / ncclAllGather instead.  The handle
+ * allocates its activation buffers once; weights and KV pages stay owned by the caller.
+ * b2d_decoder_destroy is collective when tp_size > 1 (every rank calls it). */
 B2D_API int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
                        const void* nccl_id, b2d_decoder** out);
 B2D_API int b2d_decoder_destroy(b2d_decoder* h);
+/* 1 if the steps so far use the peer-memory collectives, 0 for NCCL (or tp_size == 1). */
+B2D_API int b2d_decoder_peer_collectives(const b2d_decoder* h);
+/* Device-side status of the steps enqueued so far (synchronizes with the device): 0, or
+ * B2D_ERR_TIMEOUT if a peer barrier gave up waiting for another rank (bounded wait, 10 s).
+ * Reading clears it. */
+B2D_API int b2d_decoder_error(b2d_decoder* h);
 
 /* Weights of this rank's shard (fp16 matrices, fp32 norms), as b2d_shard_* in the Python
  * host lays them out: wqkv [(Hq+2Hkv)/tp*HD, D] rows [q | k | v] of the local heads;
@@ -306,6 +316,31 @@ B2D_API int b2d_decoder_set_head(b2d_decoder* h, const uint16_t* embed, const ui
 B2D_API int b2d_decoder_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                      const int* block_table, int batch, int* next_tokens, float* logits,
                      int use_graph, b2d_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Tensor-parallel collectives over NVLink peer memory (what the decoder runs between the
+ * row-parallel projections; no reference counterpart: the reference runs on one device).
+ * ------------------------------------------------------------------------------------- */
+
+/* x[b] += parts[0][b] + parts[1][b] + ... + parts[tp-1][b]  (rank order, so every rank computes
+ * bit-identical sums), then, if gamma != NULL, out16[b] = fp16(rmsnorm(x[b]) * gamma), for
+ * b < rows; D % 4 == 0.  parts (host array of tp device pointers) are the ranks' partial sums
+ * [rows, D] fp32, mapped into this process; sigs (host array of tp device pointers) are the
+ * ranks' signal arrays of (slot0 + rows) * 8 uint32 each, zero-initialised once; epochs
+ * (this rank's, slot0 + rows uint32, zero-initialised once) count the barrier uses per slot.
+ * Row b waits, bounded by timeout_ns, until every rank has announced its partial of row b;
+ * on timeout *err (device int) becomes B2D_ERR_TIMEOUT and that row is left unchanged. */
+B2D_API int b2d_tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs,
+                                         uint32_t* epochs, int rank, int tp, int slot0, float* x,
+                                         const float* gamma, float eps, uint16_t* out16, int D,
+                                         int rows, long long timeout_ns, int* err,
+                                         b2d_stream_t stream);
+/* tokens[b] = the index of the best (value, index) pair over the ranks' vals[r][b], idxs[r][b]
+ * (larger value, ties -> lower index), after the same bounded barrier on signal slot `slot`. */
+B2D_API int b2d_tp_argmax_gather(const float* const* vals, const int* const* idxs,
+                                 uint32_t* const* sigs, uint32_t* epochs, int rank, int tp,
+                                 int slot, int B, int* tokens, long long timeout_ns, int* err,
+                                 b2d_stream_t stream);
 
 #ifdef __cplusplus
 }

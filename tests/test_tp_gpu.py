@@ -1,7 +1,8 @@
 """Tensor-parallel decode step on 2 GPUs (NCCL) against the single-GPU oracle.
 
 Runs only where at least two GPUs are visible; each rank is a spawned process that builds its
-DecodeEngine shard, runs one step (CUDA-core path at batch 5, tensor-core path at batch 24)
+DecodeEngine shard, runs one step (CUDA-core path at batch 5, tensor-core path at batch 24),
+with the peer-memory collectives and with NCCL (B2D_TP_COLLECTIVE=nccl),
 and sends its vocab-shard logits and the combined next tokens back to the test.
 """
 
@@ -40,14 +41,14 @@ def _case(batch):
     return cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens
 
 
-def _rank(rank, world, port, batch, q):
+def _rank(rank, world, port, batch, collective, q):
     import torch.distributed as dist
     from datetime import timedelta
 
     from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, share_nccl_id
     from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), B2D_TP_COLLECTIVE=collective)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
@@ -68,7 +69,8 @@ def _rank(rank, world, port, batch, q):
         eng.step(tok, ln, tb, nxt, logits, use_graph=True)
         eng.step(tok, ln, tb, nxt, logits, use_graph=True)  # replay
         eng.stream.synchronize()
-        q.put((rank, logits.cpu().numpy(), nxt.cpu().numpy()))
+        eng.check()  # no peer barrier timed out
+        q.put((rank, logits.cpu().numpy(), nxt.cpu().numpy(), eng.peer_collectives()))
         eng.close()
         dist.barrier(device_ids=[rank])
     finally:
@@ -76,22 +78,24 @@ def _rank(rank, world, port, batch, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("collective", ["peer", "nccl"])
 @pytest.mark.parametrize("batch", [5, 24])
 @pytest.mark.timeout(600)
-def test_tp2_decode_step_matches_oracle(batch):
+def test_tp2_decode_step_matches_oracle(batch, collective):
     from oracle import step as S
     from tests._tol import assert_norm_close
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, collective, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
     for _ in range(2):
-        rank, lg, nx = q.get(timeout=500)
+        rank, lg, nx, peer = q.get(timeout=500)
         got[rank] = (lg, nx)
+        assert peer == (collective == "peer")  # the path asked for is the path that ran
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
