@@ -332,19 +332,22 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
             continue
         nmat = 2 if epi == "swiglu" else 1
         n = copies(M * K * 2 * nmat)
-        Ws = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for _ in range(n * nmat)]
+        Wr = [(torch.randn(M, K, generator=g, device=dev) * 0.02).half() for _ in range(n * nmat)]
         xh = torch.randn(B5, K, generator=g, device=dev).half()
         y = torch.zeros(B5, M, dtype=torch.float16 if epi == "swiglu" else torch.float32, device=dev)
-        if epi == "swiglu":
-            fn = lambda i: ops.gemm_tc(Ws[2 * (i % n)], xh, epilogue="swiglu", W_up=Ws[2 * (i % n) + 1], y=y)
-        elif epi == "argmax":
-            fn = lambda i: ops.gemm_tc(Ws[i % n], xh, epilogue="argmax")
-        else:
-            fn = lambda i: ops.gemm_tc(Ws[i % n], xh, epilogue=epi, y=y)
-        ms = time_launches(fn, nit(100), s)
         b = nmat * M * K * 2 + B5 * K * 2 + B5 * M * (2 if epi == "swiglu" else 4) * (2 if epi == "add" else 1)
-        res[name] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
-        del Ws
+        # the decoder's layout (packed 16 KB tiles) under the plain name, row-major as *_rowmajor
+        for key, Ws in ((name, [ops.pack_tc(w) for w in Wr]), (name + "_rowmajor", Wr)):
+            if epi == "swiglu":
+                fn = lambda i, Ws=Ws: ops.gemm_tc(Ws[2 * (i % n)], xh, epilogue="swiglu", W_up=Ws[2 * (i % n) + 1], y=y)
+            elif epi == "argmax":
+                fn = lambda i, Ws=Ws: ops.gemm_tc(Ws[i % n], xh, epilogue="argmax")
+            else:
+                fn = lambda i, Ws=Ws: ops.gemm_tc(Ws[i % n], xh, epilogue=epi, y=y)
+            ms = time_launches(fn, nit(100), s)
+            res[key] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+            del Ws
+        del Wr
     if want("c5_attn_hd64"):
         r5 = np.random.default_rng(SEED_CTX)
         lens5 = r5.integers(CTX_LO, CTX_HI + 1, size=B5).astype(np.int32)

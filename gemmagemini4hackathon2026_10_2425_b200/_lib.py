@@ -66,6 +66,9 @@ SIGNATURES = {
     "b2d_gemm_tc_workspace_bytes": (Z, [I, I, I, I]),
     "b2d_gemm_tc": (I, [P, P, P, I, I, I, P, I, P, I, I, I, P, P, P, I, P, Z, P]),
     "b2d_gemm_tc_q": (I, [I, P, P, P, I, I, I, P, I, P, I, I, I, P, Z, P]),
+    "b2d_tc_packed_bytes": (Z, [I, I]),
+    "b2d_tc_pack_f16": (I, [P, I, I, I, P, P]),
+    "b2d_gemm_tc_packed": (I, [P, P, P, I, I, I, P, I, P, I, I, I, P, P, P, I, P, Z, P]),
     "b2d_embed_f16": (I, [P, P, P, I, I, P]),
     "b2d_argmax_f32": (I, [P, I, I, P, I, P]),
     "b2d_argmax_combine": (I, [P, P, I, I, P, P]),

@@ -49,6 +49,11 @@ int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, vo
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
 int tc_gemm_q(int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
               const float*, int, int, int, void*, size_t, cudaStream_t);
+int tc_gemm_packed(const uint8_t*, const uint8_t*, const uint16_t*, int, int, int, void*, int,
+                   const float*, int, int, int, float*, int*, float*, int, void*, size_t,
+                   cudaStream_t);
+size_t tc_packed_bytes(int, int);
+int tc_pack_f16(const uint16_t*, int, int, int, void*, cudaStream_t);
 int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
                              float*, const float*, float, uint16_t*, int, int, long long, int*,
                              cudaStream_t);
@@ -185,6 +190,22 @@ int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int 
                 size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm(W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits, tokens,
                  max_vals, index_offset, workspace, workspace_bytes, S(stream));
+}
+
+size_t b2d_tc_packed_bytes(int M, int K) { return tc_packed_bytes(M, K); }
+
+int b2d_tc_pack_f16(const uint16_t* W, int ldw, int M, int K, void* out, b2d_stream_t stream) {
+  return tc_pack_f16(W, ldw, M, K, out, S(stream));
+}
+
+int b2d_gemm_tc_packed(const void* Wp, const void* Wp_up, const uint16_t* X, int ldx,
+                       int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+                       int K, int batch, float* logits, int* tokens, float* max_vals,
+                       int index_offset, void* workspace, size_t workspace_bytes,
+                       b2d_stream_t stream) {
+  return tc_gemm_packed(static_cast<const uint8_t*>(Wp), static_cast<const uint8_t*>(Wp_up), X,
+                        ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits, tokens,
+                        max_vals, index_offset, workspace, workspace_bytes, S(stream));
 }
 
 int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X, int ldx,

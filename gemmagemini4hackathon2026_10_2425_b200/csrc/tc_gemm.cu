@@ -59,11 +59,40 @@ struct Params {
   int* tokens;
   float* max_vals;
   int index_offset;
-  float* am_val;             // [m_tiles][N]
-  int* am_idx;
+  unsigned long long* am_key;  // [N] running best (value, row) key per token, zero between calls
   unsigned int* am_counter;
   const uint16_t* scales;    // quantized weights: fp16 [M, K/32]
+  // fp16 weights pre-packed into 16 KB tiles (tc_pack_f16), read with 1D bulk copies instead
+  // of the tensor maps tmA / tmA2 (nullptr: row-major weights through the tensor maps)
+  const uint8_t* pA;
+  const uint8_t* pA2;
 };
+
+// (value, row) -> 64-bit key whose unsigned order is "larger value, then lower row": the high
+// word is the float's bits made monotone, the low word is ~row.  NaN maps below -inf.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+  uint32_t u = __float_as_uint(v);
+  u = (v != v) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+  return ((unsigned long long)u << 32) | (uint32_t)(~(uint32_t)row);
+}
+__device__ __forceinline__ int argmax_key_row(unsigned long long k) {
+  return (int)(~(uint32_t)(k & 0xffffffffull));
+}
+__device__ __forceinline__ float argmax_key_value(unsigned long long k) {
+  const uint32_t u = (uint32_t)(k >> 32);
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+// One 128 x 64 fp16 weight tile: row-major [M, K] through its tensor map (128-byte rows, one
+// per weight row), or the packed tile (16 KB contiguous, already in the 128-byte-swizzled
+// shared-memory image).
+__device__ __forceinline__ void load_a_tile(void* dst, const CUtensorMap* tm, const uint8_t* packed,
+                                            int m_tile, int k_tiles, int kt, uint64_t* bar) {
+  if (packed)
+    bulk_load(dst, packed + ((size_t)m_tile * k_tiles + kt) * (BM * BK * 2), BM * BK * 2, bar);
+  else
+    tma_load_2d(dst, tm, kt * BK, m_tile * BM, bar);
+}
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
@@ -141,7 +170,9 @@ struct Cfg {
   static constexpr int B_OFF = A_BYTES * (DUAL ? 2 : 1);
   // fp16 weights: one ring of STAGES x [A | (A_up) | B], filled by TMA
   static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
-  static constexpr int STAGES = DUAL ? 4 : 8;  // one CTA per SM, deep TMA ring
+  // non-dual: 4 stages (~100 KB) so two CTAs share an SM and one streams while the other
+  // runs its prologue or epilogue; dual (gate/up, 36 KB stages): one CTA per SM
+  static constexpr int STAGES = 4;
   // quantized weights: a deep ring of RS raw tiles (the HBM stream) and a shallow ring of AS
   // operand stages [A fp16 | B] that the dequant warps fill
   static constexpr int RAW_ROW = QUANT == 1 ? BK : (QUANT == 2 ? BK / 2 : 0);  // bytes per row
@@ -218,8 +249,9 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       for (int i = 0; i < first; ++i) {
         uint8_t* st = smem + i * C::STAGE_BYTES;
         mbar_expect_tx(&full_bar[i], C::STAGE_BYTES);
-        tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[i]);
-        if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[i]);
+        load_a_tile(st, &p.tmA, p.pA, m_tile, p.k_tiles, kt_begin + i, &full_bar[i]);
+        if (DUAL)
+          load_a_tile(st + C::A_BYTES, &p.tmA2, p.pA2, m_tile, p.k_tiles, kt_begin + i, &full_bar[i]);
       }
     }
   }
@@ -275,8 +307,9 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         }
         uint8_t* st = smem + s * C::STAGE_BYTES;
         mbar_expect_tx(&full_bar[s], C::STAGE_BYTES);
-        tma_load_2d(st, &p.tmA, (kt_begin + i) * BK, m0, &full_bar[s]);
-        if (DUAL) tma_load_2d(st + C::A_BYTES, &p.tmA2, (kt_begin + i) * BK, m0, &full_bar[s]);
+        load_a_tile(st, &p.tmA, p.pA, m_tile, p.k_tiles, kt_begin + i, &full_bar[s]);
+        if (DUAL)
+          load_a_tile(st + C::A_BYTES, &p.tmA2, p.pA2, m_tile, p.k_tiles, kt_begin + i, &full_bar[s]);
         tma_load_2d(st + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[s]);
       }
     }
@@ -529,7 +562,9 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       }
     }
     __syncthreads();
-    if (tid < N) {
+    // the tile's winner per token joins the grid-wide maximum of (value, -row) keys: one 64-bit
+    // atomicMax per token and tile, order-independent (deterministic), no serial merge at the end
+    if (tid < N && tid < p.batch) {
       float bv = am_v[0][tid];
       int bi = am_i[0][tid];
       for (int w = 1; w < 4; ++w)
@@ -537,8 +572,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
           bv = am_v[w][tid];
           bi = am_i[w][tid];
         }
-      p.am_val[(size_t)m_tile * N + tid] = bv;
-      p.am_idx[(size_t)m_tile * N + tid] = bi;
+      if (bi != 0x7fffffff) atomicMax(p.am_key + tid, argmax_key(bv, bi));
     }
     __threadfence();
     __syncthreads();
@@ -546,22 +580,10 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    for (int t = warp; t < p.batch; t += 4) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int mt = lane; mt < p.m_tiles; mt += 32) {
-        const float v = __ldcg(p.am_val + (size_t)mt * N + t);
-        const int i = __ldcg(p.am_idx + (size_t)mt * N + t);
-        if (better(v, i, bv, bi)) {
-          bv = v;
-          bi = i;
-        }
-      }
-      warp_argmax(bv, bi);
-      if (lane == 0) {
-        p.tokens[t] = bi + p.index_offset;
-        if (p.max_vals) p.max_vals[t] = bv;
-      }
+    if (tid < p.batch) {
+      const unsigned long long key = atomicExch(p.am_key + tid, 0ull);  // read, and reset
+      p.tokens[tid] = argmax_key_row(key) + p.index_offset;
+      if (p.max_vals) p.max_vals[tid] = argmax_key_value(key);
     }
     if (tid == 0) *p.am_counter = 0u;
   } else {
@@ -649,7 +671,7 @@ constexpr int kMaxTiles = 4096;  // row tiles per call: M <= 4096 * 128
 
 struct TcPlan {
   int n_tile, m_tiles, k_tiles, k_splits, nacc;
-  size_t off_amv, off_ami, total;
+  size_t off_key, total;
 };
 
 static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
@@ -660,15 +682,10 @@ static TcPlan tc_plan(int M, int K, int batch, int epilogue) {
   pl.nacc = epilogue == B2D_EPI_SWIGLU ? 2 : 1;
   pl.k_splits = 1;  // chosen at launch (tc_pick_splits): it depends on cluster residency
   auto a256 = [](size_t n) { return (n + 255) / 256 * 256; };
-  // [0] error word, [64] argmax arrival counter, [256...) argmax partials (value, index)
+  // [0] error word, [64] argmax arrival counter, [256, 512) argmax keys (one u64 per token)
   size_t o = 256;
-  pl.off_amv = o;
-  pl.off_ami = o;
-  if (epilogue == B2D_EPI_ARGMAX) {
-    o += a256((size_t)pl.m_tiles * pl.n_tile * 4);
-    pl.off_ami = o;
-    o += a256((size_t)pl.m_tiles * pl.n_tile * 4);
-  }
+  pl.off_key = o;
+  if (epilogue == B2D_EPI_ARGMAX) o += a256((size_t)32 * 8);
   pl.total = o;
   return pl;
 }
@@ -774,7 +791,8 @@ struct TcCall {
 int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
                     int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
                     int K, int batch, float* logits, int* tokens, float* max_vals,
-                    int index_offset, void* workspace, size_t workspace_bytes) {
+                    int index_offset, void* workspace, size_t workspace_bytes,
+                    bool packed = false) {
   if (!call || !W || !X) return B2D_ERR_NULL;
   if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8 ||
       M > kMaxTiles * tc::BM)
@@ -792,8 +810,13 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   if (!aligned16(workspace)) return B2D_ERR_ALIGN;
   tc::Params& p = call->prm;
   p = tc::Params{};
-  B2D_TRY(make_tmap_f16(&p.tmA, W, M, K, K, tc::BM));
-  if (W_up) B2D_TRY(make_tmap_f16(&p.tmA2, W_up, M, K, K, tc::BM));
+  if (packed) {
+    p.pA = reinterpret_cast<const uint8_t*>(W);
+    p.pA2 = reinterpret_cast<const uint8_t*>(W_up);
+  } else {
+    B2D_TRY(make_tmap_f16(&p.tmA, W, M, K, K, tc::BM));
+    if (W_up) B2D_TRY(make_tmap_f16(&p.tmA2, W_up, M, K, K, tc::BM));
+  }
   B2D_TRY(make_tmap_f16(&p.tmB, X, batch, K, ldx, pl.n_tile));
   char* ws = static_cast<char*>(workspace);
   p.M = M;
@@ -813,8 +836,7 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   p.tokens = tokens;
   p.max_vals = max_vals;
   p.index_offset = index_offset;
-  p.am_val = reinterpret_cast<float*>(ws + pl.off_amv);
-  p.am_idx = reinterpret_cast<int*>(ws + pl.off_ami);
+  p.am_key = reinterpret_cast<unsigned long long*>(ws + pl.off_key);
   if (epilogue != B2D_EPI_ARGMAX) {
     const bool dual = epilogue == B2D_EPI_SWIGLU;
     p.k_splits = pl.n_tile == 16 ? (dual ? tc_pick_splits<16, true>(pl.m_tiles, pl.k_tiles)
@@ -854,6 +876,59 @@ int tc_gemm(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
   B2D_TRY(tc_gemm_prepare(&c, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
                           logits, tokens, max_vals, index_offset, workspace, workspace_bytes));
   return tc_gemm_launch(c, stream);
+}
+
+// Same product with the weights in the packed tile layout (tc_pack_f16).
+int tc_gemm_packed(const uint8_t* Wp, const uint8_t* Wp_up, const uint16_t* X, int ldx,
+                   int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
+                   int batch, float* logits, int* tokens, float* max_vals, int index_offset,
+                   void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  TcCall c;
+  B2D_TRY(tc_gemm_prepare(&c, reinterpret_cast<const uint16_t*>(Wp),
+                          reinterpret_cast<const uint16_t*>(Wp_up), X, ldx, epilogue, y_dtype, y,
+                          ldy, aux, M, K, batch, logits, tokens, max_vals, index_offset,
+                          workspace, workspace_bytes, true));
+  return tc_gemm_launch(c, stream);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Packed weight layout for the tensor-core GEMV: W [M, K] fp16 (row stride ldw) becomes
+// ceil(M/128) x ceil(K/64) tiles of 16 KB, tile (mt, kt) at ((mt * k_tiles) + kt) * 16 KB, each
+// holding rows mt*128.. and columns kt*64.. exactly as the MMA reads them from shared memory
+// (K-major, 128-byte swizzle: row r at (r/8)*1024 + (r%8)*128, 16-byte chunk c at c ^ (r%8));
+// rows / columns past M / K are zero.  A CTA's k-range of one row tile is one contiguous run
+// of HBM, where the row-major layout gives it 128-byte pieces of rows K*2 bytes apart.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) tc_pack_f16_kernel(const uint16_t* __restrict__ W, int M,
+                                                          int K, int ldw, int k_tiles,
+                                                          uint8_t* __restrict__ out) {
+  const int mt = blockIdx.y, kt = blockIdx.x, r = threadIdx.x;
+  const int row = mt * tc::BM + r;
+  uint8_t* tile = out + ((size_t)mt * k_tiles + kt) * (tc::BM * tc::BK * 2);
+  uint8_t* dst = tile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int col = kt * tc::BK + c * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < M && col < K) v = *reinterpret_cast<const uint4*>(W + (size_t)row * ldw + col);
+    *reinterpret_cast<uint4*>(dst + ((c ^ (r & 7)) << 4)) = v;
+  }
+}
+
+size_t tc_packed_bytes(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  return (size_t)((M + tc::BM - 1) / tc::BM) * ((K + tc::BK - 1) / tc::BK) * (tc::BM * tc::BK * 2);
+}
+
+int tc_pack_f16(const uint16_t* W, int ldw, int M, int K, void* out, cudaStream_t stream) {
+  if (!W || !out) return B2D_ERR_NULL;
+  if (M <= 0 || K <= 0 || K % 8 || ldw < K || ldw % 8 || M > kMaxTiles * tc::BM)
+    return B2D_ERR_SHAPE;
+  if (!aligned16(W) || !aligned16(out)) return B2D_ERR_ALIGN;
+  const int k_tiles = (K + tc::BK - 1) / tc::BK, m_tiles = (M + tc::BM - 1) / tc::BM;
+  tc_pack_f16_kernel<<<dim3(k_tiles, m_tiles), 128, 0, stream>>>(W, M, K, ldw, k_tiles,
+                                                                  static_cast<uint8_t*>(out));
+  return launch_status();
 }
 
 // Quantized weights (q8_32 / q4_32) on the tensor cores: STORE / ADD / GELU_MUL epilogues.

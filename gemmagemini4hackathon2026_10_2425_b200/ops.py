@@ -348,16 +348,41 @@ _WS_TC = Workspace()
 _TC_EPI = {"store": _lib.EPI_STORE, "add": _lib.EPI_ADD, "gelu_mul": _lib.EPI_GELU_MUL, "swiglu": _lib.EPI_SWIGLU, "argmax": _lib.EPI_ARGMAX}
 
 
+@dataclass
+class TcPacked:
+    """fp16 weights [M, K] in the tensor-core tile layout (b2d_tc_pack_f16): 16 KB tiles of 128
+    rows x 64 columns, already in the MMA's swizzled shared-memory image."""
+
+    buf: torch.Tensor  # uint8 [b2d_tc_packed_bytes(M, K)]
+    M: int
+    K: int
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return self.M, self.K
+
+
+def pack_tc(W: torch.Tensor) -> TcPacked:
+    """Repack fp16 W [M, K] (row-major) into the tensor-core tile layout."""
+    if W.dtype != torch.float16 or W.dim() != 2 or W.stride(1) != 1:
+        raise ValueError("pack_tc needs fp16 W [M, K] with unit column stride")
+    M, K = W.shape
+    buf = torch.empty(_lib.lib().b2d_tc_packed_bytes(M, K), dtype=torch.uint8, device=W.device)
+    _need_cuda(W, buf)
+    call("b2d_tc_pack_f16", W.data_ptr(), W.stride(0), M, K, buf.data_ptr(), _stream())
+    return TcPacked(buf, M, K)
+
+
 def tc_workspace_bytes(M: int, K: int, batch: int, epilogue: str = "store") -> int:
     return int(_lib.lib().b2d_gemm_tc_workspace_bytes(M, K, batch, _TC_EPI[epilogue]))
 
 
 def gemm_tc(
-    W: torch.Tensor,
+    W: torch.Tensor | TcPacked,
     X: torch.Tensor,
     *,
     epilogue: str = "store",
-    W_up: torch.Tensor | None = None,
+    W_up: torch.Tensor | TcPacked | None = None,
     aux: torch.Tensor | None = None,
     y: torch.Tensor | None = None,
     out_dtype: torch.dtype = torch.float32,
@@ -366,11 +391,17 @@ def gemm_tc(
     workspace: torch.Tensor | None = None,
 ):
     """Tensor-core batched GEMV (tcgen05): y[b] = epilogue(W @ X[b]) for fp16 W [M, K] and fp16
-    X [batch <= 32, K].  For 'argmax' returns tokens (and logits if asked)."""
+    X [batch <= 32, K].  For 'argmax' returns tokens (and logits if asked).  W (and W_up) may
+    be row-major or packed by pack_tc."""
     M, K = W.shape
     B = X.shape[0]
-    if W.dtype != torch.float16 or X.dtype != torch.float16 or X.shape[1] != K:
+    packed = isinstance(W, TcPacked)
+    if packed != (W_up is None or isinstance(W_up, TcPacked)) and W_up is not None:
+        raise ValueError("W and W_up must both be packed or both row-major")
+    if (not packed and W.dtype != torch.float16) or X.dtype != torch.float16 or X.shape[1] != K:
         raise ValueError("gemm_tc needs fp16 W [M, K] and fp16 X [batch, K]")
+    Wt = W.buf if packed else W
+    Wu = (W_up.buf if packed else W_up) if W_up is not None else None
     ws = workspace if workspace is not None else _WS_TC.get(tc_workspace_bytes(M, K, B, epilogue), X.device)
     tokens = logits = None
     if epilogue == "argmax":
@@ -385,11 +416,11 @@ def gemm_tc(
         if y.dtype not in _DT or tuple(y.shape) != (B, M):
             raise ValueError(f"y must be fp32/fp16 [{B}, {M}]")
         ydt = _DT[y.dtype]
-    _need_cuda(W, X, W_up, aux, y, ws, tokens, logits)
+    _need_cuda(Wt, X, Wu, aux, y, ws, tokens, logits)
     call(
-        "b2d_gemm_tc",
-        W.data_ptr(),
-        _ptr(W_up),
+        "b2d_gemm_tc_packed" if packed else "b2d_gemm_tc",
+        Wt.data_ptr(),
+        _ptr(Wu),
         X.data_ptr(),
         K,
         _TC_EPI[epilogue],

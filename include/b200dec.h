@@ -148,6 +148,23 @@ B2D_API int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t*
                         int batch, float* logits, int* tokens, float* max_vals, int index_offset,
                         void* workspace, size_t workspace_bytes, b2d_stream_t stream);
 
+/* Packed weight layout for the tensor-core GEMV (an HBM layout choice of this library; the
+ * reference's weights file is row-major, LK/convert_weights.py:60-72): W [M, K] fp16 becomes
+ * ceil(M/128) x ceil(K/64) tiles of 16 KB, tile (mt, kt) at byte ((mt * ceil(K/64)) + kt) *
+ * 16384, each the 128 x 64 block of rows mt*128.. and columns kt*64.. in the MMA's shared-memory
+ * image (row r at (r/8)*1024 + (r%8)*128, 16-byte chunk c of the row at ((c ^ (r%8)) * 16));
+ * rows / columns past M / K are zero.  Each CTA then streams contiguous HBM instead of 128-byte
+ * row pieces.  b2d_tc_pack_f16 writes it (out: b2d_tc_packed_bytes(M, K) bytes, 16-byte
+ * aligned; K % 8 == 0), and b2d_gemm_tc_packed is b2d_gemm_tc with Wp / Wp_up in this layout. */
+B2D_API size_t b2d_tc_packed_bytes(int M, int K);
+B2D_API int b2d_tc_pack_f16(const uint16_t* W, int ldw, int M, int K, void* out,
+                            b2d_stream_t stream);
+B2D_API int b2d_gemm_tc_packed(const void* Wp, const void* Wp_up, const uint16_t* X, int ldx,
+                               int epilogue, int y_dtype, void* y, int ldy, const float* aux,
+                               int M, int K, int batch, float* logits, int* tokens,
+                               float* max_vals, int index_offset, void* workspace,
+                               size_t workspace_bytes, b2d_stream_t stream);
+
 /* The tensor-core batched GEMV for 32-block quantized weights (w_dtype B2D_Q8_32 or B2D_Q4_32,
  * layouts above; scales fp16 [M, K/32]): TMA streams the raw weight tiles through a deep
  * shared-memory ring and dequantizer warps expand them to fp16(scale * q) -- the MMA operand --

@@ -168,3 +168,50 @@ def test_tc_quant_bad_arguments_raise():
     with pytest.raises(ValueError):
         ops.gemm_tc_q(Wq, d(np.zeros((4, 96), np.float16)), epilogue="swiglu")
 
+
+def np_pack_tc(W):
+    """NumPy restatement of the packed tile layout (b2d_tc_pack_f16)."""
+    M, K = W.shape
+    mt, kt = -(-M // 128), -(-K // 64)
+    Wp = np.zeros((mt * 128, kt * 64), np.float16)
+    Wp[:M, :K] = W
+    out = np.zeros((mt, kt, 128, 64), np.float16)  # tile image: [row][8 chunks of 8]
+    for r in range(128):
+        perm = [(c ^ (r % 8)) for c in range(8)]  # chunk c of row r sits at slot c ^ (r % 8)
+        src = Wp.reshape(mt, 128, kt, 64)[:, r].reshape(mt, kt, 8, 8)
+        dst = np.zeros_like(src)
+        dst[:, :, perm] = src
+        out[:, :, r] = dst.reshape(mt, kt, 64)
+    return out.reshape(-1).view(np.uint8)
+
+
+@pytest.mark.parametrize("M,K", [(256, 128), (200, 72), (1000, 520)])
+def test_tc_pack_layout_bit_exact(M, K):
+    W = np.random.default_rng(M).standard_normal((M, K)).astype(np.float16)
+    got = ops.pack_tc(d(W)).buf.cpu().numpy()
+    np.testing.assert_array_equal(got, np_pack_tc(W))
+
+
+@pytest.mark.parametrize("epi", ["store", "add", "swiglu", "argmax"])
+@pytest.mark.parametrize("M,K,b", [(3072, 2048, 32), (2048, 8192, 32), (1000, 520, 16), (200, 72, 9)])
+def test_tc_packed_equals_rowmajor(epi, M, K, b):
+    """Same tiles reach the MMA either way: results are bit-identical."""
+    W, X = case(M, K, b, 3 * M + K)
+    Wu, _ = case(M, K, b, 5 * M + K)
+    y0 = np.random.default_rng(8).standard_normal((b, M)).astype(np.float32)
+    out = []
+    for packed in (False, True):
+        Wa = ops.pack_tc(d(W)) if packed else d(W)
+        Wb = (ops.pack_tc(d(Wu)) if packed else d(Wu)) if epi == "swiglu" else None
+        if epi == "argmax":
+            tok, lg = ops.gemm_tc(Wa, d(X), epilogue="argmax", return_logits=True)
+            out.append((tok.cpu().numpy(), lg.cpu().numpy()))
+        else:
+            y = d(y0.copy())
+            r = ops.gemm_tc(Wa, d(X), epilogue=epi, W_up=Wb, y=y if epi in ("store", "add") else None)
+            out.append((r.float().cpu().numpy(),))
+    for a, c in zip(*out):
+        np.testing.assert_array_equal(a, c)
+    if epi == "store":
+        assert_rel_close(out[1][0], O.gemv(W, X), 2e-3)
+
