@@ -229,9 +229,11 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_kernel(const __grid_c
     if (blk >= 0) {
       uint8_t* dst = ring + (size_t)s2 * 2 * C::PAGE_BYTES;
       mbar_expect_tx(bar, 2 * C::PAGE_BYTES);
-      bulk_load(dst, p.k_pages + (size_t)blk * blk_stride + kv_head_off, C::PAGE_BYTES, bar);
-      bulk_load(dst + C::PAGE_BYTES, p.v_pages + (size_t)blk * blk_stride + kv_head_off,
-                C::PAGE_BYTES, bar);
+      const uint64_t pol = l2_evict_first();  // KV pages are read once per step
+      bulk_load_hint(dst, p.k_pages + (size_t)blk * blk_stride + kv_head_off, C::PAGE_BYTES, bar,
+                     pol);
+      bulk_load_hint(dst + C::PAGE_BYTES, p.v_pages + (size_t)blk * blk_stride + kv_head_off,
+                     C::PAGE_BYTES, bar, pol);
     } else {
       mbar_arrive(bar);  // nothing to load: complete the phase, the page is masked
     }
@@ -525,11 +527,12 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
     if (blk >= 0) {
       uint8_t* dst = my_ring + (k % SW) * C::STAGE_BYTES;
       const int row0 = (blk * p.n_kv_heads + kvh) * 16;
+      const uint64_t pol = l2_evict_first();  // KV pages are read once per step
       mbar_expect_tx(bar, C::STAGE_BYTES);
 #pragma unroll
       for (int bx = 0; bx < C::BOXES; ++bx) {
-        tma_load_2d(dst + bx * 2048, &p.tmK, bx * 64, row0, bar);
-        tma_load_2d(dst + C::PAGE_BYTES + bx * 2048, &p.tmV, bx * 64, row0, bar);
+        tma_load_2d_hint(dst + bx * 2048, &p.tmK, bx * 64, row0, bar, pol);
+        tma_load_2d_hint(dst + C::PAGE_BYTES + bx * 2048, &p.tmV, bx * 64, row0, bar, pol);
       }
     } else {
       mbar_arrive(bar);  // nothing to load: the page is masked

@@ -43,11 +43,15 @@ int num_sms();  // cached per device
 // ------------------------------------------------------------------------------------------
 
 // 16-byte streaming load of read-only data, not kept in L1 (weights, KV pages).
+// Streaming 16-byte load of data read once per step (weights): no L1 allocation, and evicted
+// from L2 first so it does not displace the step's small hot data.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return v;
 }
 

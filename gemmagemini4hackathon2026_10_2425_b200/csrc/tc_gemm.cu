@@ -88,10 +88,12 @@ __device__ __forceinline__ float argmax_key_value(unsigned long long k) {
 // shared-memory image).
 __device__ __forceinline__ void load_a_tile(void* dst, const CUtensorMap* tm, const uint8_t* packed,
                                             int m_tile, int k_tiles, int kt, uint64_t* bar) {
+  const uint64_t pol = l2_evict_first();  // weights are read once per step
   if (packed)
-    bulk_load(dst, packed + ((size_t)m_tile * k_tiles + kt) * (BM * BK * 2), BM * BK * 2, bar);
+    bulk_load_hint(dst, packed + ((size_t)m_tile * k_tiles + kt) * (BM * BK * 2), BM * BK * 2, bar,
+                   pol);
   else
-    tma_load_2d(dst, tm, kt * BK, m_tile * BM, bar);
+    tma_load_2d_hint(dst, tm, kt * BK, m_tile * BM, bar, pol);
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
@@ -242,8 +244,8 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     if constexpr (QUANT) {
       for (int i = 0; i < min(nkt, C::RS); ++i) {
         mbar_expect_tx(&raw_full[i], C::RAW_BYTES);
-        tma_load_2d(smem + C::RAW_RING_OFF + i * C::RAW_BYTES, &p.tmA,
-                    (kt_begin + i) * C::RAW_ROW, m0, &raw_full[i]);
+        tma_load_2d_hint(smem + C::RAW_RING_OFF + i * C::RAW_BYTES, &p.tmA,
+                         (kt_begin + i) * C::RAW_ROW, m0, &raw_full[i], l2_evict_first());
       }
     } else {
       for (int i = 0; i < first; ++i) {
@@ -290,8 +292,8 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             break;
           }
           mbar_expect_tx(&raw_full[rs], C::RAW_BYTES);
-          tma_load_2d(smem + C::RAW_RING_OFF + rs * C::RAW_BYTES, &p.tmA,
-                      (kt_begin + j) * C::RAW_ROW, m0, &raw_full[rs]);
+          tma_load_2d_hint(smem + C::RAW_RING_OFF + rs * C::RAW_BYTES, &p.tmA,
+                           (kt_begin + j) * C::RAW_ROW, m0, &raw_full[rs], l2_evict_first());
         }
       }
     } else {
