@@ -406,12 +406,13 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_kernel(const __grid_c
 // ------------------------------------------------------------------------------------------
 // Tensor-core variant (head_dim 64 / 128): every warp owns a private ring of pages loaded by
 // TMA (tiled, 128-byte swizzle) and treats one page as one warp-level MMA tile:
-//   S[h, j] = q_h . k_j  as  m16n8k16 with the G query heads as rows (padded to 16), tokens as
-//   columns; P = exp(S - m) in registers; O[h, :] += P V with P re-packed from the S
-//   accumulators as the A operand and V read with ldmatrix.trans.
-// q and p enter the fp16 MMAs as hi + lo fp16 pairs, so scores and weights keep ~22-bit
-// precision (K and V are exactly their stored fp16 values).  No CTA-wide barrier runs inside
-// the main loop; warps merge at the end like the sub-warps of the CUDA-core kernel.
+//   S[h, j] = q_h . k_j  as  m16n8k16 with the G query heads as rows, tokens as columns;
+//   P = exp(S - m) in registers; O[h, :] += P V with P re-packed from the S accumulators as
+//   the A operand and V read with ldmatrix.trans.
+// q and p enter each MMA as hi + lo fp16 pairs -- hi parts in rows 0..7, lo parts in rows
+// 8..15 of the same 16-row tile (mma_hilo) -- so scores and weights keep ~22-bit precision at
+// one MMA per tile (K and V are exactly their stored fp16 values).  No CTA-wide barrier runs
+// inside the main loop; warps merge at the end like the sub-warps of the CUDA-core kernel.
 // ------------------------------------------------------------------------------------------
 
 template <int HD>
@@ -444,14 +445,17 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
-// D += A(16x16, rows g / g+8) * B(16x8); a1 = a3 = 0 (rows 8..15 are padding here).
-__device__ __forceinline__ void mma_rows8(float* d, uint32_t a0, uint32_t a2, uint32_t b0,
-                                          uint32_t b1) {
+// D += A(16x16) * B(16x8) with the hi parts of the G <= 8 live rows in rows 0..7 and their lo
+// parts (x - fp16(x)) in rows 8..15: d[0], d[1] accumulate the hi products and d[2], d[3] the
+// lo products of the same (row, column) pairs, so d[0] + d[2] and d[1] + d[3] carry ~22-bit
+// operand precision from one fp16 MMA (the reference computes q.k and p.v in fp32).
+__device__ __forceinline__ void mma_hilo(float* d, uint32_t hi0, uint32_t lo0, uint32_t hi2,
+                                         uint32_t lo2, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+      : "r"(hi0), "r"(lo0), "r"(hi2), "r"(lo2), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
@@ -646,14 +650,12 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
       const uint32_t addr = kbase + (ch / 8) * 2048 + trow * 128 + (((ch % 8) ^ (trow & 7)) << 4);
       uint32_t b00, b01, b10, b11;
       ldsm_x4(addr, b00, b01, b10, b11);
-      mma_rows8(s0, qa[ks][0], qa[ks][1], b00, b01);
-      mma_rows8(s0, qb[ks][0], qb[ks][1], b00, b01);
-      mma_rows8(s1, qa[ks][0], qa[ks][1], b10, b11);
-      mma_rows8(s1, qb[ks][0], qb[ks][1], b10, b11);
+      mma_hilo(s0, qa[ks][0], qb[ks][0], qa[ks][1], qb[ks][1], b00, b01);
+      mma_hilo(s1, qa[ks][0], qb[ks][0], qa[ks][1], qb[ks][1], b10, b11);
     }
     // online softmax for row g over this page's 16 tokens (4 per thread, quad of lanes)
     const int j0 = pg * 16 + 2 * t4;
-    float sv[4] = {s0[0], s0[1], s1[0], s1[1]};
+    float sv[4] = {s0[0] + s0[2], s0[1] + s0[3], s1[0] + s1[2], s1[1] + s1[3]};
     const int jj[4] = {j0, j0 + 1, j0 + 8, j0 + 9};
     float mx = -INFINITY;
 #pragma unroll
@@ -680,6 +682,8 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
     for (int nd = 0; nd < ND; ++nd) {
       o[nd][0] *= corr;
       o[nd][1] *= corr;
+      o[nd][2] *= corr;
+      o[nd][3] *= corr;
     }
     uint32_t ph0, pl0, ph2, pl2;
     split_h2(pe[0], pe[1], ph0, pl0);
@@ -693,10 +697,8 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
       const uint32_t addr = vbase + (ch / 8) * 2048 + tok * 128 + (((ch % 8) ^ (tok & 7)) << 4);
       uint32_t v0, v1, v2, v3;
       ldsm_x4_t(addr, v0, v1, v2, v3);
-      mma_rows8(o[nd], ph0, ph2, v0, v1);
-      mma_rows8(o[nd], pl0, pl2, v0, v1);
-      mma_rows8(o[nd + 1], ph0, ph2, v2, v3);
-      mma_rows8(o[nd + 1], pl0, pl2, v2, v3);
+      mma_hilo(o[nd], ph0, pl0, ph2, pl2, v0, v1);
+      mma_hilo(o[nd + 1], ph0, pl0, ph2, pl2, v2, v3);
     }
     __syncwarp();
     if (lane == 0 && k + SW < my_n) {
@@ -718,8 +720,8 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
     float* sp = st + ((size_t)warp * G + g) * (HD + 2);
 #pragma unroll
     for (int nd = 0; nd < ND; ++nd) {
-      sp[8 * nd + 2 * t4] = o[nd][0];
-      sp[8 * nd + 2 * t4 + 1] = o[nd][1];
+      sp[8 * nd + 2 * t4] = o[nd][0] + o[nd][2];
+      sp[8 * nd + 2 * t4 + 1] = o[nd][1] + o[nd][3];
     }
     if (t4 == 0) {
       sp[HD] = m;

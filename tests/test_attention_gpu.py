@@ -174,3 +174,14 @@ def test_workspace_shared_across_batch_shapes():
         )
         ro, _, _ = run_oracle(c, hq, hk, 128, 10000.0)
         assert_rel_close(out.cpu().numpy(), ro, 2e-3)
+
+
+def test_large_batch_many_short_sequences():
+    """300 short sequences (one chunk each, most CTAs of the grid idle): same results."""
+    r = np.random.default_rng(300)
+    lens = r.integers(0, 40, size=300).tolist()
+    c = make_case(lens, 32, 8, 64, seed=301, extra_blocks=2)
+    go, gk, gv = run_gpu(c, 32, 8, 64, 500000.0)
+    ro, rk, rv = run_oracle(c, 32, 8, 64, 500000.0)
+    assert_rel_close(go, ro, 2e-3)
+    check_pages(gk, gv, rk, rv)
