@@ -35,6 +35,11 @@ CTX_LO, CTX_HI = 512, 4096
 SEED_W, SEED_KV, SEED_CTX, SEED_TOK = 1234, 99, 7, 3
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
+# DRAM bytes per launch from one ncu capture of each kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum); commands and figures in profiles/paged_attn_c5_hd64.md and
+# profiles/tc_gemm_gateup_c5.md
+ATTN_C5_TRAFFIC = 160_088_832 + 4_641_024
+GATEUP_TRAFFIC = 67_329_280 + 683_264
 
 
 def peaks() -> tuple[float, str]:
@@ -376,7 +381,7 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
         )
         tot = int((lens5 + 1).sum())
         b = tot * hk5 * hd5 * 2 * 2 + B5 * (hq5 + 2 * hk5) * hd5 * 4 + B5 * hq5 * hd5 * 2 + 4 * sum(need5)
-        res["c5_attn_hd64"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+        res["c5_attn_hd64"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak, "bytes": b}
         del pools
     # config 4: ragged paged attention
     if not want("c4_paged_attn_64seq"):
@@ -557,8 +562,23 @@ def run_ours(args) -> None:
     if rank == 0 and world == 1 and not args.no_ops:
         res = op_benchmarks(peak)
         out["ops"] = res
-        # dominant kernel of the step: the tcgen05 gate/up SwiGLU GEMM at batch 32, rotating over
-        # the 16 layers' weights (1 GB > L2) so every launch streams its weights from HBM
+        # dominant kernel of the step (a third of its launch-list time): the paged attention of one
+        # layer, timed above in op_benchmarks as "c5_attn_hd64" (rotating KV pools > 2x L2)
+        att = res["c5_attn_hd64"]
+        out["roofline"] = {
+            "kernel": "paged_attn_tc_kernel<64,4> (one layer of config 5: 32 seqs, ctx U[512,4096], 32/8 heads, HD 64, KV append)",
+            "bound": "hbm",
+            "achieved": att["gbs"],
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": att["frac"],
+            "traffic": ATTN_C5_TRAFFIC,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/paged_attn_c5_hd64.md",
+            "bytes_per_launch": att["bytes"],
+            "us_per_launch": att["us"],
+        }
+        # second kernel family: the tcgen05 gate/up SwiGLU projection at batch 32
         L0 = eng.layers
         xh = torch.randn(BATCH, shape.dim, device=dev).half()
         h = torch.empty(BATCH, shape.ffn_dim // world, dtype=torch.float16, device=dev)
@@ -569,15 +589,14 @@ def run_ours(args) -> None:
         )
         fl = shape.ffn_dim // world
         kb = 2 * fl * shape.dim * 2 + BATCH * shape.dim * 2 + BATCH * fl * 2
-        out["roofline"] = {
-            "kernel": "tc_gemm_kernel<N=32, SWIGLU> (tcgen05 gate/up projection, batch 32)",
+        out["roofline_gemm"] = {
+            "kernel": "tc_gemm_kernel<32, SWIGLU> (tcgen05 gate/up projection, batch 32)",
             "bound": "hbm",
             "achieved": kb / ms_k / 1e6,
             "peak": peak,
-            "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": kb / ms_k / 1e6 / peak,
-            "traffic": None,
+            "traffic": GATEUP_TRAFFIC,
             "bytes_per_launch": kb,
             "us_per_launch": ms_k * 1e3,
         }
