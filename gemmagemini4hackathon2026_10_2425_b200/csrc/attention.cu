@@ -490,7 +490,9 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
   __shared__ int cta_failed;
 
   const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  pdl_wait();
+  // Context lengths, the block table and the cached pages are inputs of the step that no kernel
+  // of the step writes before this one, so everything up to the first ring of page copies runs
+  // before griddepcontrol.wait, overlapping the tail of the QKV projection.
   const int pos = p.ctx_lens[b];
   if (pos < 0 || pos >= p.max_ctx) return;  // outside the caller's contract: output untouched
   const int n = pos + 1;
@@ -544,6 +546,7 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
   };
   if (lane == 0)
     for (int k = 0; k < min(my_n, SW); ++k) issue(k);
+  pdl_wait();  // q, k, v of the new token come from the previous kernel
 
   // rotated, pre-scaled q and the new token's k / v (as in the CUDA-core kernel)
   const size_t row = (size_t)b * p.ldqkv;
