@@ -415,12 +415,23 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_kernel(const __grid_c
 // inside the main loop; warps merge at the end like the sub-warps of the CUDA-core kernel.
 // ------------------------------------------------------------------------------------------
 
+// Pages in flight per warp of the tensor-core kernel.  Fewer stages mean less shared memory per
+// CTA and more CTAs (warps) per SM, which beat deeper rings on B200: head_dim 64 at 2 stages
+// (6 CTAs per SM) 34.2 us for the config-5 layer vs 36.9 at 3 and 41.0 at 4; head_dim 128 at 2
+// stages (3 CTAs per SM) 203 us for config 4 vs 217 at 1 and 229 at 3.
+#ifndef B2D_ATTN_STAGES_HD64
+#define B2D_ATTN_STAGES_HD64 2
+#endif
+#ifndef B2D_ATTN_STAGES_HD128
+#define B2D_ATTN_STAGES_HD128 2
+#endif
+
 template <int HD>
 struct TcAttnCfg {
   static constexpr int WARPS = kAttnThreads / 32;     // 4
   static constexpr int BOXES = HD / 64;               // 64-column TMA boxes per page slice
   static constexpr int PAGE_BYTES = 16 * HD * 2;      // one KV head's K (or V) page slice
-  static constexpr int SW = HD == 64 ? 4 : 3;         // stages per warp
+  static constexpr int SW = HD == 64 ? B2D_ATTN_STAGES_HD64 : B2D_ATTN_STAGES_HD128;  // per warp
   static constexpr int STAGE_BYTES = 2 * PAGE_BYTES;  // K slice, then V slice
   static constexpr int WARP_RING = SW * STAGE_BYTES;
   static constexpr int RING = WARPS * WARP_RING;

@@ -186,7 +186,9 @@ struct Cfg {
   static constexpr int NACC = DUAL ? 2 : 1;
   // split-K receive buffer (not aliased with the ring: peers write into it while this CTA may
   // still be streaming): [source rank][acc][token][owned rows + pad], owned rows = BM / splits
-  static constexpr int RED_FLOATS = NACC * N * (BM + 4 * 8);
+  // split-K receive buffer: [source rank][accumulator][owned row][N + 4] (padded rows: the
+  // 16-byte reads of consecutive rows fall in distinct banks); ks x (BM / ks) = BM rows in all
+  static constexpr int RED_FLOATS = NACC * BM * (N + 4);
   static constexpr int SMEM = RING_BYTES + RED_FLOATS * 4 + 1024;  // + alignment slack
   static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
 };
@@ -477,39 +479,46 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     const int ks = p.k_splits;
     const int rank = (int)cl.block_rank();
     const int own_rows = BM / ks;
-    const int old_ = own_rows + 4;  // padded row stride of the receive buffer
+    constexpr int NP = N + 4;  // padded row of the receive buffer (floats)
     float* red = reinterpret_cast<float*>(smem + C::RING_BYTES);
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every peer has started
     if (ok && epi_warp) {
+      // this thread's row of partial sums (N tokens) goes to its owner as N/4 16-byte stores
       const int sl = r / 16, owner = sl % ks;
       const int lr = (sl / ks) * 16 + (r % 16);
       float* dst = cl.map_shared_rank(red, owner);
+      float4* d0 = reinterpret_cast<float4*>(dst + ((rank * C::NACC + 0) * own_rows + lr) * NP);
 #pragma unroll
-      for (int t = 0; t < N; ++t) {
-        dst[((rank * C::NACC + 0) * N + t) * old_ + lr] = acc[t];
-        if (DUAL) dst[((rank * C::NACC + 1) * N + t) * old_ + lr] = acc2[t];
+      for (int t = 0; t < N; t += 4) d0[t / 4] = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+      if constexpr (DUAL) {
+        float4* d1 = reinterpret_cast<float4*>(dst + ((rank * C::NACC + 1) * own_rows + lr) * NP);
+#pragma unroll
+        for (int t = 0; t < N; t += 4)
+          d1[t / 4] = make_float4(acc2[t], acc2[t + 1], acc2[t + 2], acc2[t + 3]);
       }
     }
-    // prefetch what the epilogue reads from global memory while the barrier completes
-    constexpr int MAXV = N / 2;  // values per thread for k_splits >= 2
-    float yv[DUAL ? 1 : MAXV];
+    // each owner thread then finishes items of (one owned row, 4 consecutive tokens); prefetch
+    // what those items read from global memory while the barrier completes
+    constexpr int MAXQ = N / 8;  // items per thread (k_splits >= 2)
+    float yv[DUAL ? 1 : MAXQ][4];
     pdl_wait();
     pdl_launch_dependents();
-    const int nv = own_rows * N;
+    const int nq = own_rows * (N / 4);
     if (!DUAL && ok && epi_warp && (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL)) {
 #pragma unroll
-      for (int k = 0; k < MAXV; ++k) {
+      for (int k = 0; k < MAXQ; ++k) {
         const int v = etid + k * THREADS;
-        yv[k] = 0.f;
-        if (v < nv) {
-          const int lr = v % own_rows, t = v / own_rows;
-          const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
-          if (t < p.batch && grow < p.M) {
-            const size_t yi = (size_t)t * p.ldy + grow;
-            yv[k] = p.epi == B2D_EPI_GELU_MUL
-                        ? p.aux[yi]
-                        : (p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
-                                   : reinterpret_cast<const float*>(p.y)[yi]);
+        const int lr = v % own_rows, t0 = 4 * (v / own_rows);
+        const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          yv[k][j] = 0.f;
+          if (v < nq && t0 + j < p.batch && grow < p.M) {
+            const size_t yi = (size_t)(t0 + j) * p.ldy + grow;
+            yv[k][j] = p.epi == B2D_EPI_GELU_MUL
+                           ? p.aux[yi]
+                           : (p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
+                                      : reinterpret_cast<const float*>(p.y)[yi]);
           }
         }
       }
@@ -517,30 +526,46 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     cl.sync();  // every partial row has reached its owner
     if (ok && epi_warp) {
 #pragma unroll
-      for (int k = 0; k < MAXV; ++k) {
+      for (int k = 0; k < MAXQ; ++k) {
         const int v = etid + k * THREADS;
-        if (v >= nv) break;
-        const int lr = v % own_rows, t = v / own_rows;
+        if (v >= nq) break;
+        const int lr = v % own_rows, t0 = 4 * (v / own_rows);
         const int grow = m0 + ((lr / 16) * ks + rank) * 16 + (lr % 16);
-        float a = 0.f, a2 = 0.f;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), a2 = a;
         for (int q = 0; q < ks; ++q) {  // fixed source order: deterministic sums
-          a += red[((q * C::NACC + 0) * N + t) * old_ + lr];
-          if (DUAL) a2 += red[((q * C::NACC + 1) * N + t) * old_ + lr];
+          const float4 u = *reinterpret_cast<const float4*>(red + ((q * C::NACC + 0) * own_rows + lr) * NP + t0);
+          a.x += u.x;
+          a.y += u.y;
+          a.z += u.z;
+          a.w += u.w;
+          if constexpr (DUAL) {
+            const float4 u2 = *reinterpret_cast<const float4*>(red + ((q * C::NACC + 1) * own_rows + lr) * NP + t0);
+            a2.x += u2.x;
+            a2.y += u2.y;
+            a2.z += u2.z;
+            a2.w += u2.w;
+          }
         }
-        if (t >= p.batch || grow >= p.M) continue;
-        const size_t yi = (size_t)t * p.ldy + grow;
-        float y;
-        if (DUAL) {
-          y = silu(a) * a2;
-        } else {
-          y = a;
-          if (p.epi == B2D_EPI_ADD) y += yv[k];
-          else if (p.epi == B2D_EPI_GELU_MUL) y = gelu_tanh(y) * yv[k];
+        if (grow >= p.M) continue;
+        const float av[4] = {a.x, a.y, a.z, a.w}, a2v[4] = {a2.x, a2.y, a2.z, a2.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int t = t0 + j;
+          if (t >= p.batch) break;
+          const size_t yi = (size_t)t * p.ldy + grow;
+          float y;
+          if constexpr (DUAL) {
+            y = silu(av[j]) * a2v[j];
+          } else {
+            y = av[j];
+            if (p.epi == B2D_EPI_ADD) y += yv[k][j];
+            else if (p.epi == B2D_EPI_GELU_MUL) y = gelu_tanh(y) * yv[k][j];
+          }
+          if (p.y_f16)
+            reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
+          else
+            reinterpret_cast<float*>(p.y)[yi] = y;
         }
-        if (p.y_f16)
-          reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
-        else
-          reinterpret_cast<float*>(p.y)[yi] = y;
       }
     }
     return;
