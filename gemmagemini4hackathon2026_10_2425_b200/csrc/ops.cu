@@ -148,6 +148,20 @@ int add_f32(float* x, const float* p, size_t n, cudaStream_t stream) {
 //   if p: x += p (written back);   out = fp16(x * rsqrt(mean(x^2) + eps) * gamma)
 // (rmsnorm LK/kernels.metal:71-89; the add is the residual update after a tensor-parallel
 // all-reduce).  Launched with programmatic dependent launch.
+// Row width handled from registers: up to kNormVec float4 per thread (D <= 4096 at 256 threads);
+// wider or unaligned rows take the scalar loop.
+constexpr int kNormVec = 4;
+
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  return t;
+}
+
 __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const float* p,
                                                               const float* gamma, float eps,
                                                               uint16_t* out, int D) {
@@ -156,6 +170,51 @@ __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const fl
   float* xr = x + (size_t)blockIdx.x * D;
   const float* pr = p ? p + (size_t)blockIdx.x * D : nullptr;
   uint16_t* orow = out + (size_t)blockIdx.x * D;
+  const bool vec = (D & 3) == 0 && D <= kNormVec * 4 * 256 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma) |
+                     reinterpret_cast<uintptr_t>(p)) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+  if (vec) {
+    // all loads of the row issued before the first use: one memory latency, not D/256 of them
+    float4 v[kNormVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormVec; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (4 * i < D) {
+        v[k] = reinterpret_cast<const float4*>(xr)[i];
+        if (pr) {
+          const float4 a = reinterpret_cast<const float4*>(pr)[i];
+          v[k].x += a.x;
+          v[k].y += a.y;
+          v[k].z += a.z;
+          v[k].w += a.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kNormVec; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (4 * i < D) {
+        if (pr) reinterpret_cast<float4*>(xr)[i] = v[k];
+        ss = fmaf(v[k].x, v[k].x, fmaf(v[k].y, v[k].y, fmaf(v[k].z, v[k].z, fmaf(v[k].w, v[k].w, ss))));
+      }
+    }
+    const float scale = rsqrtf(block_sum_256(ss, red) / (float)D + eps);
+    pdl_launch_dependents();
+#pragma unroll
+    for (int k = 0; k < kNormVec; ++k) {
+      const int i = threadIdx.x + k * 256;
+      if (4 * i < D) {
+        const float4 g = reinterpret_cast<const float4*>(gamma)[i];
+        const __half2 lo = __floats2half2_rn(v[k].x * scale * g.x, v[k].y * scale * g.y);
+        const __half2 hi = __floats2half2_rn(v[k].z * scale * g.z, v[k].w * scale * g.w);
+        reinterpret_cast<uint2*>(orow)[i] =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+      }
+    }
+    return;
+  }
   float ss = 0.f;
   for (int i = threadIdx.x; i < D; i += 256) {
     float v = xr[i];
@@ -165,12 +224,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const fl
     }
     ss = fmaf(v, v, ss);
   }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  const float scale = rsqrtf(tot / (float)D + eps);
+  const float scale = rsqrtf(block_sum_256(ss, red) / (float)D + eps);
   pdl_launch_dependents();
   for (int i = threadIdx.x; i < D; i += 256) orow[i] = f2h(xr[i] * scale * gamma[i]);
 }

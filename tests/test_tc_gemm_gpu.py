@@ -94,14 +94,16 @@ def test_tc_error_word_stays_zero():
     assert int(ws[:4].view(torch.int32).item()) == 0
 
 
-def test_add_rmsnorm_f16():
-    r = np.random.default_rng(1)
-    x = r.standard_normal((5, 2048)).astype(np.float32)
-    p = r.standard_normal((5, 2048)).astype(np.float32)
-    g = (1 + 0.1 * r.standard_normal(2048)).astype(np.float32)
+@pytest.mark.parametrize("D", [2048, 64, 4096, 4100, 2050])  # vector path; > 4096 or odd: scalar
+@pytest.mark.parametrize("with_p", [True, False])
+def test_add_rmsnorm_f16(D, with_p):
+    r = np.random.default_rng(D)
+    x = r.standard_normal((5, D)).astype(np.float32)
+    p = r.standard_normal((5, D)).astype(np.float32) if with_p else np.zeros((5, D), np.float32)
+    g = (1 + 0.1 * r.standard_normal(D)).astype(np.float32)
     xt = d(x.copy())
-    out = ops.add_rmsnorm_f16(xt, d(g), 1e-5, p=d(p))
-    np.testing.assert_allclose(xt.cpu().numpy(), x + p, rtol=1e-6)
+    out = ops.add_rmsnorm_f16(xt, d(g), 1e-5, p=d(p) if with_p else None)
+    np.testing.assert_array_equal(xt.cpu().numpy(), x + p)  # fp32 add, bit-exact
     assert_rel_close(out.float().cpu().numpy(), O.rmsnorm(x + p, g, 1e-5), 2e-3)
 
 
