@@ -49,6 +49,8 @@ int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, 
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
+int tc_gemm_multi_store(const uint16_t*, const uint16_t*, int, float* const*, int, int, int, int,
+                        int, void*, size_t, cudaStream_t);
 int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
                              float*, const float*, float, uint16_t*, int, int, long long, int*,
                              cudaStream_t);
@@ -120,7 +122,9 @@ struct b2d_decoder {
   bool peer = false;                   // peer-memory collectives (else NCCL)
   void* peer_arena = nullptr;          // this rank's shared buffers
   void* peer_open[kMaxTp] = {};        // peers' arenas mapped here (nullptr for this rank)
-  float* parts[2][kMaxTp] = {};        // row-parallel partials [B, D], two alternating buffers
+  // row-parallel partial sums [B, D], two alternating buffers: recv[buf][owner][src] is the
+  // slot in rank `owner`'s memory that holds rank `src`'s partial (mapped here over IPC)
+  float* recv[2][kMaxTp][kMaxTp] = {};
   float* am_val[kMaxTp] = {};          // LM-head (max, index) per token [B]
   int* am_idx[kMaxTp] = {};
   uint32_t* sigs[kMaxTp] = {};         // signal arrays [(B + 1) slots][kMaxTp]
@@ -141,15 +145,35 @@ static int cuda_status(cudaError_t e) {
 
 static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
-// Sum the ranks' row-parallel partials (buffer `buf`) into the residual x; with gamma, also
-// write fp16(rmsnorm(x) * gamma) to out16.
-static int tp_reduce(b2d_decoder* h, int buf, const float* gamma, uint16_t* out16, int B,
-                     cudaStream_t s) {
+// Row-parallel projection (tensor cores) of this rank into buffer `buf`: with peer memory the
+// epilogue stores the partial straight into every rank's receive slot for this rank (the data
+// crosses NVLink while the GEMM finishes), else into the local slot for NCCL.
+static int tp_partial(b2d_decoder* h, int buf, const uint16_t* W, const uint16_t* X, int K, int B,
+                      cudaStream_t s) {
   const int D = h->cfg.dim;
-  if (h->peer)
-    return tp_allreduce_add_rmsnorm(h->parts[buf], h->sigs, h->epochs, h->rank, h->tp, 0, h->x,
-                                    gamma, h->cfg.eps, out16, D, B, kPeerTimeoutNs, h->err, s);
-  float* mine = h->parts[buf][h->rank];
+  if (h->peer) {
+    float* ys[kMaxTp];
+    for (int r = 0; r < h->tp; ++r) ys[r] = h->recv[buf][r][h->rank];
+    return tc_gemm_multi_store(W, X, K, ys, h->tp, D, D, K, B, h->tc_ws, h->tc_ws_bytes, s);
+  }
+  return tc_gemm(W, nullptr, X, K, B2D_EPI_STORE, B2D_F32, h->recv[buf][h->rank][h->rank], D,
+                 nullptr, D, K, B, nullptr, nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
+}
+
+// Sum the ranks' row-parallel partials (buffer `buf`) into the residual x; with gamma, also
+// write fp16(rmsnorm(x) * gamma) to out16.  `pushed`: every rank's producer already stored its
+// partial into this rank's receive slots (the tensor-core path), so the sum reads local memory;
+// otherwise each rank's partial sits in its own slot and the sum reads it over NVLink.
+static int tp_reduce(b2d_decoder* h, int buf, const float* gamma, uint16_t* out16, int B,
+                     bool pushed, cudaStream_t s) {
+  const int D = h->cfg.dim;
+  if (h->peer) {
+    float* parts[kMaxTp];
+    for (int r = 0; r < h->tp; ++r) parts[r] = pushed ? h->recv[buf][h->rank][r] : h->recv[buf][r][r];
+    return tp_allreduce_add_rmsnorm(parts, h->sigs, h->epochs, h->rank, h->tp, 0, h->x, gamma,
+                                    h->cfg.eps, out16, D, B, kPeerTimeoutNs, h->err, s);
+  }
+  float* mine = h->recv[buf][h->rank][h->rank];
   B2D_TRY(nccl_status(ncclAllReduce(mine, mine, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
   return gamma ? add_rmsnorm_f16(h->x, mine, gamma, h->cfg.eps, out16, B, D, s)
                : add_f32(h->x, mine, (size_t)B * D, s);
@@ -196,9 +220,8 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                       HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, B, D, s));
     } else {
-      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_STORE, B2D_F32, h->parts[0][h->rank],
-                      D, nullptr, D, HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-      B2D_TRY(tp_reduce(h, 0, L.ffn_norm, h->xn16, B, s));
+      B2D_TRY(tp_partial(h, 0, L.wo, h->att16, HQD, B, s));
+      B2D_TRY(tp_reduce(h, 0, L.ffn_norm, h->xn16, B, h->peer, s));
     }
     // gate/up SwiGLU (column-parallel) -> fp16
     B2D_TRY(tc_gemm(L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, B2D_F16, h->h16, h->fl, nullptr,
@@ -209,10 +232,8 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                       h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, B, D, s));
     } else {
-      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_STORE, B2D_F32,
-                      h->parts[1][h->rank], D, nullptr, D, h->fl, B, nullptr, nullptr, nullptr, 0,
-                      ws, wsb, s));
-      B2D_TRY(tp_reduce(h, 1, next_norm, h->xn16, B, s));
+      B2D_TRY(tp_partial(h, 1, L.wdown, h->h16, h->fl, B, s));
+      B2D_TRY(tp_reduce(h, 1, next_norm, h->xn16, B, h->peer, s));
     }
   }
   // LM head (vocab-parallel) + argmax
@@ -258,8 +279,8 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
     } else {
       B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
                             h->hq * HD, nullptr, 0.f, B2D_EPI_STORE, B2D_F32,
-                            h->parts[0][h->rank], D, nullptr, D, h->hq * HD, B, s));
-      B2D_TRY(tp_reduce(h, 0, nullptr, nullptr, B, s));
+                            h->recv[0][h->rank][h->rank], D, nullptr, D, h->hq * HD, B, s));
+      B2D_TRY(tp_reduce(h, 0, nullptr, nullptr, B, false, s));
     }
     // RMSNorm + gate/up SwiGLU (column-parallel: this rank's FFN rows)
     B2D_TRY(gemv_dispatch(B2D_F16, L.wgate, nullptr, L.wup, nullptr, B2D_F32, h->x, D,
@@ -272,9 +293,9 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                             s));
     } else {
       B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
-                            nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->parts[1][h->rank], D,
+                            nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->recv[1][h->rank][h->rank], D,
                             nullptr, D, h->fl, B, s));
-      B2D_TRY(tp_reduce(h, 1, nullptr, nullptr, B, s));
+      B2D_TRY(tp_reduce(h, 1, nullptr, nullptr, B, false, s));
     }
   }
   // final RMSNorm + LM head (vocab-parallel) + argmax
@@ -291,15 +312,16 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
   return B2D_OK;
 }
 
-// Tensor-parallel buffers that the peers read: partials (2 x [B, D] fp32), LM-head (max, index)
-// [B] and the signal array.  With CUDA IPC every rank maps every peer's allocation (handles are
+// Tensor-parallel buffers shared with the peers: receive slots for every rank's partial sums
+// (2 x tp x [B, D] fp32), LM-head (max, index) [B] and the signal array.  With CUDA IPC every rank maps every peer's allocation (handles are
 // exchanged with one ncclAllGather); if any rank cannot, or B2D_TP_COLLECTIVE=nccl, all ranks
 // keep their buffers local and use NCCL collectives instead (decided together: ncclMin).
 static int setup_peers(b2d_decoder* h) {
   const int B = h->cfg.max_batch, D = h->cfg.dim, tp = h->tp;
   const size_t part_b = align256((size_t)B * D * 4), am_b = align256((size_t)B * 4);
   const size_t sig_b = align256((size_t)(B + 1) * kMaxTp * 4);
-  const size_t total = 2 * part_b + 2 * am_b + sig_b;
+  const size_t recv_b = 2 * (size_t)tp * part_b;
+  const size_t total = recv_b + 2 * am_b + sig_b;
   B2D_TRY(cuda_status(cudaMalloc(&h->peer_arena, total)));
   B2D_TRY(cuda_status(cudaMemset(h->peer_arena, 0, total)));
   B2D_TRY(cuda_status(cudaDeviceSynchronize()));  // signals are zero before any peer can write
@@ -347,11 +369,12 @@ static int setup_peers(b2d_decoder* h) {
   for (int r = 0; r < tp; ++r) {
     char* b = h->peer ? base[r] : (r == h->rank ? base[r] : nullptr);
     if (!b) continue;
-    h->parts[0][r] = reinterpret_cast<float*>(b);
-    h->parts[1][r] = reinterpret_cast<float*>(b + part_b);
-    h->am_val[r] = reinterpret_cast<float*>(b + 2 * part_b);
-    h->am_idx[r] = reinterpret_cast<int*>(b + 2 * part_b + am_b);
-    h->sigs[r] = reinterpret_cast<uint32_t*>(b + 2 * part_b + 2 * am_b);
+    for (int buf = 0; buf < 2; ++buf)
+      for (int src = 0; src < tp; ++src)
+        h->recv[buf][r][src] = reinterpret_cast<float*>(b + ((size_t)buf * tp + src) * part_b);
+    h->am_val[r] = reinterpret_cast<float*>(b + recv_b);
+    h->am_idx[r] = reinterpret_cast<int*>(b + recv_b + am_b);
+    h->sigs[r] = reinterpret_cast<uint32_t*>(b + recv_b + 2 * am_b);
   }
   if (!h->peer)
     for (int r = 0; r < kMaxTp; ++r)

@@ -66,7 +66,25 @@ struct Params {
   // of the tensor maps tmA / tmA2 (nullptr: row-major weights through the tensor maps)
   const uint8_t* pA;
   const uint8_t* pA2;
+  // STORE epilogue into several fp32 copies of y (n_ys > 0, then y is unused): tensor-parallel
+  // partial sums pushed straight into every rank's receive buffer over NVLink
+  float* ys[8];
+  int n_ys;
 };
+
+// y[yi] = v into y, or into every copy in p.ys
+template <typename P>
+__device__ __forceinline__ void store_y(const P& p, size_t yi, float v) {
+  if (p.n_ys > 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < p.n_ys) p.ys[i][yi] = v;
+  } else if (p.y_f16) {
+    reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(v);
+  } else {
+    reinterpret_cast<float*>(p.y)[yi] = v;
+  }
+}
 
 // (value, row) -> 64-bit key whose unsigned order is "larger value, then lower row": the high
 // word is the float's bits made monotone, the low word is ~row.  NaN maps below -inf.
@@ -561,10 +579,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             if (p.epi == B2D_EPI_ADD) y += yv[k][j];
             else if (p.epi == B2D_EPI_GELU_MUL) y = gelu_tanh(y) * yv[k][j];
           }
-          if (p.y_f16)
-            reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(y);
-          else
-            reinterpret_cast<float*>(p.y)[yi] = y;
+          store_y(p, yi, y);
         }
       }
     }
@@ -630,10 +645,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         else if (p.epi == B2D_EPI_GELU_MUL)
           v = gelu_tanh(v) * p.aux[yi];
       }
-      if (p.y_f16)
-        reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(v);
-      else
-        reinterpret_cast<float*>(p.y)[yi] = v;
+      store_y(p, yi, v);
     }
   }
 }
@@ -819,7 +831,7 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
                     int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
                     int K, int batch, float* logits, int* tokens, float* max_vals,
                     int index_offset, void* workspace, size_t workspace_bytes,
-                    bool packed = false) {
+                    bool packed = false, float* const* ys = nullptr, int n_ys = 0) {
   if (!call || !W || !X) return B2D_ERR_NULL;
   if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8 ||
       M > kMaxTiles * tc::BM)
@@ -829,7 +841,9 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   if (epilogue == B2D_EPI_SWIGLU && !W_up) return B2D_ERR_NULL;
   if (epilogue == B2D_EPI_GELU_MUL && !aux) return B2D_ERR_NULL;
   if (epilogue == B2D_EPI_ARGMAX && !tokens) return B2D_ERR_NULL;
-  if (epilogue != B2D_EPI_ARGMAX && !y) return B2D_ERR_NULL;
+  if (epilogue != B2D_EPI_ARGMAX && !y && n_ys == 0) return B2D_ERR_NULL;
+  if (n_ys < 0 || n_ys > 8 || (n_ys > 0 && (!ys || epilogue != B2D_EPI_STORE || y_dtype != B2D_F32)))
+    return B2D_ERR_UNSUPPORTED;
   if (epilogue != B2D_EPI_ARGMAX && ldy < M) return B2D_ERR_SHAPE;
   if (!aligned16(W) || !aligned16(X) || (W_up && !aligned16(W_up))) return B2D_ERR_ALIGN;
   const TcPlan pl = tc_plan(M, K, batch, epilogue);
@@ -864,6 +878,11 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   p.max_vals = max_vals;
   p.index_offset = index_offset;
   p.am_key = reinterpret_cast<unsigned long long*>(ws + pl.off_key);
+  p.n_ys = n_ys;
+  for (int i = 0; i < n_ys; ++i) {
+    if (!ys[i]) return B2D_ERR_NULL;
+    p.ys[i] = ys[i];
+  }
   if (epilogue != B2D_EPI_ARGMAX) {
     const bool dual = epilogue == B2D_EPI_SWIGLU;
     p.k_splits = pl.n_tile == 16 ? (dual ? tc_pick_splits<16, true>(pl.m_tiles, pl.k_tiles)
@@ -902,6 +921,18 @@ int tc_gemm(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
   TcCall c;
   B2D_TRY(tc_gemm_prepare(&c, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
                           logits, tokens, max_vals, index_offset, workspace, workspace_bytes));
+  return tc_gemm_launch(c, stream);
+}
+
+// STORE of the fp32 product into n_ys copies (row stride ldy each), e.g. every tensor-parallel
+// rank's receive buffer.
+int tc_gemm_multi_store(const uint16_t* W, const uint16_t* X, int ldx, float* const* ys, int n_ys,
+                        int ldy, int M, int K, int batch, void* workspace, size_t workspace_bytes,
+                        cudaStream_t stream) {
+  TcCall c;
+  B2D_TRY(tc_gemm_prepare(&c, W, nullptr, X, ldx, B2D_EPI_STORE, B2D_F32, nullptr, ldy, nullptr, M,
+                          K, batch, nullptr, nullptr, nullptr, 0, workspace, workspace_bytes, false,
+                          ys, n_ys));
   return tc_gemm_launch(c, stream);
 }
 

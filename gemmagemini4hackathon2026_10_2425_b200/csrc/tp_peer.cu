@@ -8,21 +8,24 @@
 //   x[b] += part_0[b] + part_1[b] + ... + part_{tp-1}[b]        (rank order: every rank gets
 //   out16[b] = fp16(rmsnorm(x[b]) * gamma)                        bit-identical results)
 //
-// One CTA per token row.  Each rank's partials live in a buffer that every peer has mapped
-// (CUDA IPC); a CTA announces "my partial of row b is ready" by writing an epoch number into
-// every peer's signal array, waits (bounded) until all peers' epochs for row b have arrived in
-// its own array, then reads row b of every rank's partial over NVLink.  Per-row barriers, no
-// grid-wide synchronization, no NCCL launch, and the residual add + RMSNorm kernel that would
-// follow the all-reduce is gone.
+// One CTA per token row.  The partials live in buffers every rank has mapped (CUDA IPC).  With
+// the tensor-core projections each rank's GEMM epilogue has already stored its partial into
+// every rank's receive slot (remote stores overlap the GEMM's tail), so the sum reads local
+// memory; otherwise each rank's partial sits in its own memory and is read over NVLink.  A CTA
+// announces "my partial of row b is complete" by writing an epoch number into every peer's
+// signal array, waits (bounded) until all peers' epochs for row b have arrived in its own
+// array, then sums.  Per-row barriers, no grid-wide synchronization, no NCCL launch, and the
+// residual add + RMSNorm kernel that would follow the all-reduce is gone.
 //
 // The vocab-parallel LM head ends the same way: each rank's (max logit, index) per token is
 // gathered from the peers and combined (ties -> lowest index), replacing two all-gathers and a
 // combine kernel.
 //
-// Buffer reuse: the decoder alternates two partial buffers (O -> 0, down -> 1).  A rank
-// rewrites buffer k only after it has passed the barrier of the use in between, which every
-// peer reaches only after finishing its reads of buffer k (each kernel waits for its
-// predecessor with griddepcontrol.wait before doing anything that depends on it).
+// Buffer reuse: the decoder alternates two sets of partial buffers (O -> 0, down -> 1).  A rank
+// writes set k again (locally or into a peer's receive slots) only after it has passed the
+// barrier of the use in between, which every peer reaches only after finishing its reads of set
+// k (each kernel waits for its predecessor with griddepcontrol.wait before doing anything that
+// depends on it).
 #include <cstdint>
 
 #include "common.cuh"
@@ -49,18 +52,24 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-// Per-slot barrier among the tp ranks.  Returns false (CTA-uniform) if some peer did not
-// arrive within timeout_ns; *err then holds B2D_ERR_TIMEOUT.
+// Per-slot barrier among the tp ranks.  Thread r < tp announces this rank to rank r and then
+// waits for rank r's announcement.  The data a rank announces was written by the previous kernel
+// on that rank (its partial in its own memory, or pushed into the peers' receive slots): that
+// grid has completed -- its stores, remote ones included, are performed -- before this kernel
+// passes griddepcontrol.wait and writes the flag, so the flag needs no release fence, and the
+// readers fetch the data with L1-bypassing loads after the wait and a CTA barrier.  System-scope
+// fences cost ~9 us per launch here (measured), which is why they are avoided.  Returns false
+// (CTA-uniform) if some peer did not arrive within timeout_ns; *err then holds B2D_ERR_TIMEOUT.
 __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, uint32_t* epochs,
                              long long timeout_ns, int* err) {
   __shared__ uint32_t epoch_s;
@@ -68,23 +77,25 @@ __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, u
     const uint32_t e = epochs[slot] + 1u;
     epochs[slot] = e;
     epoch_s = e;
-    __threadfence_system();  // this rank's partial (written before this kernel) first
-    for (int p = 0; p < tp; ++p) st_release_sys(sig[p] + slot * kSigStride + rank, e);
   }
   __syncthreads();
   const uint32_t e = epoch_s;
   bool ok = true;
   if (threadIdx.x < tp) {
-    const uint32_t* mine = sig[rank] + slot * kSigStride + threadIdx.x;
-    const uint64_t t0 = global_ns();
-    while ((int)(ld_acquire_sys(mine) - e) < 0) {
-      if ((long long)(global_ns() - t0) > timeout_ns) {
-        ok = false;
-        atomicExch(err, B2D_ERR_TIMEOUT);
-        break;
+    const int r = threadIdx.x;
+    st_relaxed_sys(sig[r] + slot * kSigStride + rank, e);
+    const uint32_t* mine = sig[rank] + slot * kSigStride + r;
+    if ((int)(ld_volatile(mine) - e) < 0) {
+      const uint64_t t0 = global_ns();
+      while ((int)(ld_volatile(mine) - e) < 0) {
+        if ((long long)(global_ns() - t0) > timeout_ns) {
+          ok = false;
+          atomicExch(err, B2D_ERR_TIMEOUT);
+          break;
+        }
       }
-      __nanosleep(32);
     }
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   return __syncthreads_and(ok) != 0;
 }

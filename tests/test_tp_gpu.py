@@ -1,6 +1,6 @@
-"""Tensor-parallel decode step on 2 GPUs (NCCL) against the single-GPU oracle.
+"""Tensor-parallel decode step on 2, 4 and 8 GPUs against the single-GPU oracle.
 
-Runs only where at least two GPUs are visible; each rank is a spawned process that builds its
+Each world size runs only where that many GPUs are visible; each rank is a spawned process that builds its
 DecodeEngine shard, runs one step (CUDA-core path at batch 5, tensor-core path at batch 24),
 with the peer-memory collectives and with NCCL (B2D_TP_COLLECTIVE=nccl),
 and sends its vocab-shard logits and the combined next tokens back to the test.
@@ -77,22 +77,25 @@ def _rank(rank, world, port, batch, collective, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize(
+    "world",
+    [pytest.param(w, marks=pytest.mark.skipif(torch.cuda.device_count() < w, reason=f"needs {w} GPUs")) for w in (2, 4, 8)],
+)
 @pytest.mark.parametrize("collective", ["peer", "nccl"])
 @pytest.mark.parametrize("batch", [5, 24])
 @pytest.mark.timeout(600)
-def test_tp2_decode_step_matches_oracle(batch, collective):
+def test_tp_decode_step_matches_oracle(batch, collective, world):
     from oracle import step as S
     from tests._tol import assert_norm_close
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, batch, collective, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, batch, collective, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
-    for _ in range(2):
+    for _ in range(world):
         rank, lg, nx, peer = q.get(timeout=500)
         got[rank] = (lg, nx)
         assert peer == (collective == "peer")  # the path asked for is the path that ran
@@ -101,7 +104,8 @@ def test_tp2_decode_step_matches_oracle(batch, collective):
         assert p.exitcode == 0
     cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens = _case(batch)
     ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, kp, vp)
-    logits = np.concatenate([got[0][0], got[1][0]], axis=1)
-    assert_norm_close(logits, ref_logits, 2e-3, what=f"tp2 logits b{batch}")
-    np.testing.assert_array_equal(got[0][1], got[1][1])  # every rank agrees on the tokens
+    logits = np.concatenate([got[r][0] for r in range(world)], axis=1)
+    assert_norm_close(logits, ref_logits, 2e-3, what=f"tp{world} logits b{batch}")
+    for r in range(1, world):
+        np.testing.assert_array_equal(got[0][1], got[r][1])  # every rank agrees on the tokens
     np.testing.assert_array_equal(got[0][1], np.argmax(logits, axis=1))
