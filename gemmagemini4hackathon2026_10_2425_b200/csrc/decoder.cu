@@ -133,6 +133,10 @@ struct b2d_decoder {
   // graph cache
   cudaGraphExec_t gexec = nullptr;
   GraphKey gkey;
+  // device-resident decode loop (b2d_decoder_generate): step + advance, captured once
+  int* gen_next = nullptr;  // [B] next tokens of the loop's step
+  cudaGraphExec_t gen_exec = nullptr;
+  GraphKey gen_key;
 };
 
 static int nccl_status(ncclResult_t r) { return r == ncclSuccess ? B2D_OK : B2D_ERR_NCCL; }
@@ -248,6 +252,21 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
   return B2D_OK;
+}
+
+// Device-resident loop: after a step, the next tokens become the inputs of the following step,
+// every position advances by one, and the tokens are appended to a ring the host reads later.
+__global__ void advance_kernel(int* tokens, int* ctx_lens, const int* next, int* ring,
+                               int* ring_count, int ring_steps, int B) {
+  const int row = *ring_count % ring_steps;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int t = next[b];
+    tokens[b] = t;
+    ctx_lens[b] += 1;
+    ring[(size_t)row * B + b] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *ring_count += 1;
 }
 
 // Enqueue one decode step on `s` (no synchronization, graph-capturable).
@@ -449,7 +468,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   size_t sizes[] = {
       (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,
       (size_t)B * h->fl * 4,      (size_t)(B + 1) * 4,      (size_t)c.head_dim / 2 * 4,
-      (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)4,
+      (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)4,  (size_t)B * 4,
       h->attn_ws_bytes,           h->am_ws_bytes,
       (size_t)B * D * 2,          (size_t)B * h->hq * c.head_dim * 2, (size_t)B * h->fl * 2,
       h->tc_ws_bytes};
@@ -465,6 +484,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
   void** slots[] = {(void**)&h->x,        (void**)&h->qkv,      (void**)&h->att,
                     (void**)&h->hid,      (void**)&h->epochs,   (void**)&h->invf,
                     (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->err,
+                    (void**)&h->gen_next,
                     (void**)&h->attn_ws,  (void**)&h->am_ws,
                     (void**)&h->xn16,     (void**)&h->att16,    (void**)&h->h16,
                     (void**)&h->tc_ws};
@@ -497,6 +517,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
 int b2d_decoder_destroy(b2d_decoder* h) {
   if (!h) return B2D_OK;
   if (h->gexec) cudaGraphExecDestroy(h->gexec);
+  if (h->gen_exec) cudaGraphExecDestroy(h->gen_exec);
   if (h->comm && h->peer) {
     // every rank stops reading its peers' buffers before any rank frees its own
     cudaDeviceSynchronize();
@@ -510,6 +531,13 @@ int b2d_decoder_destroy(b2d_decoder* h) {
   if (h->arena) cudaFree(h->arena);
   delete h;
   return B2D_OK;
+}
+
+int b2d_decoder_set_inv_freq(b2d_decoder* h, const float* inv_freq_host, int n) {
+  if (!h || !inv_freq_host) return B2D_ERR_NULL;
+  if (n != h->cfg.head_dim / 2) return B2D_ERR_SHAPE;
+  // same device buffer: a captured step graph picks the new values up
+  return cuda_status(cudaMemcpy(h->invf, inv_freq_host, (size_t)n * 4, cudaMemcpyHostToDevice));
 }
 
 int b2d_decoder_peer_collectives(const b2d_decoder* h) { return h && h->peer ? 1 : 0; }
@@ -537,6 +565,11 @@ int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,
     h->gexec = nullptr;
     h->gkey = GraphKey();
   }
+  if (h->gen_exec) {
+    cudaGraphExecDestroy(h->gen_exec);
+    h->gen_exec = nullptr;
+    h->gen_key = GraphKey();
+  }
   return B2D_OK;
 }
 
@@ -552,6 +585,11 @@ int b2d_decoder_set_head(b2d_decoder* h, const uint16_t* embed, const uint16_t* 
     cudaGraphExecDestroy(h->gexec);
     h->gexec = nullptr;
     h->gkey = GraphKey();
+  }
+  if (h->gen_exec) {
+    cudaGraphExecDestroy(h->gen_exec);
+    h->gen_exec = nullptr;
+    h->gen_key = GraphKey();
   }
   return B2D_OK;
 }
@@ -593,6 +631,51 @@ int b2d_decoder_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
     h->gkey = key;
   }
   return cuda_status(cudaGraphLaunch(h->gexec, s));
+}
+
+int b2d_decoder_generate(b2d_decoder* h, int* tokens, int* ctx_lens, const int* block_table,
+                         int batch, int n_steps, int* ring, int ring_steps, int* ring_count,
+                         b2d_stream_t stream) {
+  if (!h) return B2D_ERR_NULL;
+  if (!tokens || !ctx_lens || !block_table || !ring || !ring_count) return B2D_ERR_NULL;
+  if (batch <= 0 || batch > h->cfg.max_batch || n_steps < 0 || ring_steps <= 0)
+    return B2D_ERR_SHAPE;
+  if (!h->embed) return B2D_ERR_STATE;
+  for (const Layer& L : h->layers)
+    if (!L.wqkv) return B2D_ERR_STATE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (s == nullptr) return B2D_ERR_STATE;  // the legacy default stream cannot be captured
+  GraphKey key;
+  key.batch = batch * 65536 + ring_steps;
+  key.stream = s;
+  const void* ptrs[6] = {tokens, ctx_lens, block_table, ring, ring_count, nullptr};
+  for (int i = 0; i < 6; ++i) key.ptrs[i] = ptrs[i];
+  if (!h->gen_exec || !(key == h->gen_key)) {
+    if (h->gen_exec) {
+      cudaGraphExecDestroy(h->gen_exec);
+      h->gen_exec = nullptr;
+    }
+    B2D_TRY(cuda_status(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal)));
+    int st = enqueue_step(h, tokens, ctx_lens, block_table, batch, h->gen_next, nullptr, s);
+    if (st == B2D_OK) {
+      advance_kernel<<<1, 256, 0, s>>>(tokens, ctx_lens, h->gen_next, ring, ring_count,
+                                       ring_steps, batch);
+      st = launch_status();
+    }
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &graph);
+    if (st != B2D_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      return st;
+    }
+    B2D_TRY(cuda_status(e));
+    e = cudaGraphInstantiate(&h->gen_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    B2D_TRY(cuda_status(e));
+    h->gen_key = key;
+  }
+  for (int i = 0; i < n_steps; ++i) B2D_TRY(cuda_status(cudaGraphLaunch(h->gen_exec, s)));
+  return B2D_OK;
 }
 
 }  // extern "C"

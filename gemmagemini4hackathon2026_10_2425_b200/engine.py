@@ -146,7 +146,8 @@ class DecodeEngine:
                 self.v_pages[i].data_ptr(),
             )
         self.embed = w["embed"].to(dev).half().contiguous()
-        self.lm_head = tpmod.shard_head(self.embed, s, self.rank, self.tp)
+        head = w["lm_head"].to(dev).half().contiguous() if "lm_head" in w else self.embed
+        self.lm_head = tpmod.shard_head(head, s, self.rank, self.tp)
         self.final_norm = w["final_norm"].to(dev).float().contiguous()
         call(
             "b2d_decoder_set_head",
@@ -156,6 +157,29 @@ class DecodeEngine:
             self.lm_rows,
             self.final_norm.data_ptr(),
         )
+
+    def set_inv_freq(self, inv_freq) -> None:
+        """RoPE inverse frequencies (head_dim / 2 floats), e.g. weights.inv_freq_from_config()."""
+        import numpy as np
+
+        a = np.ascontiguousarray(np.asarray(inv_freq, dtype=np.float32))
+        call("b2d_decoder_set_inv_freq", self._h, a.ctypes.data, a.size)
+
+    def load_weights_file(self, path) -> dict:
+        """Load a weights file in the reference's format (weights.py) into this rank's shards
+        and apply its RoPE settings; returns the file's config.  Needs alloc_kv() first."""
+        from . import weights as W
+
+        wf = W.read_weights(path)
+        shape = W.shape_from_config(wf.config)
+        if shape != self.shape:
+            raise ValueError(f"{path}: model shape {shape} does not match this engine's {self.shape}")
+        import numpy as np
+
+        # the mapped file is read-only: each tensor is copied once on its way to the device
+        self.load_weights({k: torch.from_numpy(np.array(v)) for k, v in W.tensors_for_engine(wf).items()})
+        self.set_inv_freq(W.inv_freq_from_config(wf.config))
+        return wf.config
 
     def random_weights(self, seed: int, std: float = 0.02) -> None:
         """Seeded random-init weights generated on the device (fp16 ~ N(0, std), norms = 1).
@@ -217,6 +241,41 @@ class DecodeEngine:
             self.stream.cuda_stream,
         )
         return next_tokens
+
+    def generate(
+        self,
+        tokens: torch.Tensor,
+        ctx_lens: torch.Tensor,
+        block_table: torch.Tensor,
+        n_steps: int,
+        ring: torch.Tensor | None = None,
+        ring_count: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """Enqueue n_steps greedy decode steps that feed each other on the device (no host sync).
+        tokens / ctx_lens (int32 [B], device) advance in place; returns the ring [n_steps, B] the
+        generated tokens land in (pass ring / ring_count to keep appending to your own)."""
+        B = tokens.numel()
+        for t in (tokens, ctx_lens, block_table):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("tokens, ctx_lens, block_table: contiguous CUDA int32")
+        if ring is None:
+            ring = torch.zeros(max(n_steps, 1), B, dtype=torch.int32, device=tokens.device)
+        if ring_count is None:
+            ring_count = torch.zeros(1, dtype=torch.int32, device=tokens.device)
+        call(
+            "b2d_decoder_generate",
+            self._h,
+            tokens.data_ptr(),
+            ctx_lens.data_ptr(),
+            block_table.data_ptr(),
+            B,
+            n_steps,
+            ring.data_ptr(),
+            ring.shape[0],
+            ring_count.data_ptr(),
+            self.stream.cuda_stream,
+        )
+        return ring
 
     def peer_collectives(self) -> bool:
         """True if the tensor-parallel sums run over NVLink peer memory (False: NCCL or tp 1)."""

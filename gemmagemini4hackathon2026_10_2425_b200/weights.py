@@ -1,0 +1,147 @@
+"""The reference's flat weights file: reader, writer and model configuration.
+
+Format (written by the reference's converter, LK/convert_weights.py:1-94; read by its engine,
+LK/main.swift:113-148):
+
+    [0:8)     little-endian u64 = header length H
+    [8:8+H)   UTF-8 JSON header {"config": <HF config.json>, "tensors": {name: {"offset", "shape",
+              "dtype"}}}
+    ...       tensor data; every tensor starts on a 256-byte boundary (absolute offsets); the file
+              is padded to a 16 KiB multiple
+
+Tensor names: embed, l{i}.attn_norm, l{i}.wqkv (rows [q | k | v]), l{i}.wo, l{i}.ffn_norm,
+l{i}.wgate, l{i}.wup, l{i}.wdown, final_norm, and lm_head when the embeddings are not tied; fp16
+matrices, fp32 norms.  Files of this format load directly into DecodeEngine
+(`DecodeEngine.load_weights_file`), sharded per tensor-parallel rank on the way.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from .tp import ModelShape
+
+ALIGN = 256
+PAGE = 16384
+HEADER_RESERVE = 64 * 1024  # the reference converter's fixed header prefix
+
+
+@dataclass
+class WeightsFile:
+    config: dict
+    tensors: dict[str, np.ndarray]  # read-only views of the mapped file
+    path: Path
+
+
+def read_weights(path: str | Path) -> WeightsFile:
+    """Map a weights file; tensors are zero-copy views (np.memmap)."""
+    path = Path(path)
+    raw = np.memmap(path, dtype=np.uint8, mode="r")
+    if raw.size < 8:
+        raise ValueError(f"{path}: too short for a weights file")
+    hlen = int(np.frombuffer(raw[:8].tobytes(), "<u8")[0])
+    if 8 + hlen > raw.size:
+        raise ValueError(f"{path}: header length {hlen} exceeds the file")
+    header = json.loads(raw[8 : 8 + hlen].tobytes().decode("utf-8"))
+    tensors = {}
+    for name, meta in header["tensors"].items():
+        dt = np.dtype(meta["dtype"])
+        shape = tuple(int(d) for d in meta["shape"])
+        off = int(meta["offset"])
+        n = int(np.prod(shape)) * dt.itemsize
+        if off % ALIGN or off + n > raw.size:
+            raise ValueError(f"{path}: tensor {name} at {off} (+{n} B) is misaligned or out of range")
+        tensors[name] = raw[off : off + n].view(dt).reshape(shape)
+    return WeightsFile(header["config"], tensors, path)
+
+
+def write_weights(path: str | Path, config: dict, tensors: dict[str, np.ndarray]) -> int:
+    """Write tensors (in the given order) in the reference's layout; returns the file size."""
+    off = HEADER_RESERVE
+    meta = {}
+    for name, arr in tensors.items():
+        off = -(-off // ALIGN) * ALIGN
+        meta[name] = {"offset": off, "shape": list(arr.shape), "dtype": str(arr.dtype)}
+        off += arr.nbytes
+    total = -(-off // PAGE) * PAGE
+    header = json.dumps({"config": config, "tensors": meta}).encode()
+    if 8 + len(header) > HEADER_RESERVE:
+        raise ValueError("header does not fit the reserved prefix")
+    with open(path, "wb") as f:
+        f.write(len(header).to_bytes(8, "little"))
+        f.write(header)
+        for name, arr in tensors.items():
+            f.seek(meta[name]["offset"])
+            f.write(np.ascontiguousarray(arr).tobytes())
+        f.truncate(total)
+    return total
+
+
+def _rope(cfg: dict) -> tuple[float, dict]:
+    """(rope_theta, scaling dict) from either config style: top-level rope_theta / rope_scaling
+    (the Hub's Llama-3.2 config.json, as LK/main.swift:89-96 reads it) or the newer
+    rope_parameters block that holds both."""
+    rp = cfg.get("rope_parameters") or {}
+    theta = cfg.get("rope_theta", rp.get("rope_theta"))
+    if theta is None:
+        raise KeyError("config has neither rope_theta nor rope_parameters.rope_theta")
+    scaling = cfg.get("rope_scaling") or (rp if rp.get("rope_type", "default") != "default" else {})
+    return float(theta), scaling or {}
+
+
+def shape_from_config(cfg: dict) -> ModelShape:
+    """HF config.json fields -> the decode step's shape (LK/main.swift:78-87)."""
+    d = int(cfg["hidden_size"])
+    nh = int(cfg["num_attention_heads"])
+    return ModelShape(
+        dim=d,
+        n_layers=int(cfg["num_hidden_layers"]),
+        n_heads=nh,
+        n_kv_heads=int(cfg["num_key_value_heads"]),
+        head_dim=int(cfg.get("head_dim") or d // nh),
+        ffn_dim=int(cfg["intermediate_size"]),
+        vocab=int(cfg["vocab_size"]),
+        eps=float(cfg["rms_norm_eps"]),
+        theta=_rope(cfg)[0],
+    )
+
+
+def inv_freq_from_config(cfg: dict) -> np.ndarray:
+    """RoPE inverse frequencies in float64, then fp32, with Llama-3 scaling when the config asks
+    for it (LK/main.swift:89-108; the published Llama-3 rule: wavelengths shorter than
+    orig_ctx / high_freq_factor keep their frequency, longer than orig_ctx / low_freq_factor are
+    divided by `factor`, and the band between is interpolated linearly in orig_ctx / wavelength)."""
+    shape = shape_from_config(cfg)
+    hd, theta = shape.head_dim, shape.theta
+    inv = [1.0 / theta ** (2 * i / hd) for i in range(hd // 2)]
+    rs = _rope(cfg)[1]
+    if rs.get("rope_type", rs.get("type")) == "llama3":
+        factor = float(rs["factor"])
+        lo, hi = float(rs["low_freq_factor"]), float(rs["high_freq_factor"])
+        old = float(rs["original_max_position_embeddings"])
+        out = []
+        for f in inv:
+            wavelen = 2 * math.pi / f
+            if wavelen < old / hi:
+                out.append(f)
+            elif wavelen > old / lo:
+                out.append(f / factor)
+            else:
+                smooth = (old / wavelen - lo) / (hi - lo)
+                out.append((1 - smooth) * f / factor + smooth * f)
+        inv = out
+    return np.asarray(inv, dtype=np.float64).astype(np.float32)
+
+
+def tensors_for_engine(wf: WeightsFile) -> dict[str, np.ndarray]:
+    """The file's tensors under the names DecodeEngine.load_weights takes (lm_head falls back to
+    the tied embedding)."""
+    t = dict(wf.tensors)
+    if "lm_head" not in t:
+        t["lm_head"] = t["embed"]
+    return t

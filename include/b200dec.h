@@ -307,6 +307,19 @@ B2D_API int b2d_nccl_get_unique_id(void* out_host);
 B2D_API int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
                        const void* nccl_id, b2d_decoder** out);
 B2D_API int b2d_decoder_destroy(b2d_decoder* h);
+/* Device-resident greedy decode loop: n_steps decode steps back to back with no host round trip.
+ * After each step the next tokens replace tokens[b], ctx_lens[b] grows by one, and the tokens
+ * are written to ring row (*ring_count % ring_steps), ring [ring_steps][batch] int32, after which
+ * *ring_count grows by one (all device memory; tokens and ctx_lens are updated in place).  The
+ * caller keeps ctx_lens + n_steps within max_ctx and the block table covering them.  The step
+ * and the advance are captured into one CUDA graph (per pointer set) and launched n_steps times
+ * (the reference's pipelined decode loop, LK/main.swift:473-491, with sampling kept on the GPU). */
+B2D_API int b2d_decoder_generate(b2d_decoder* h, int* tokens, int* ctx_lens, const int* block_table,
+                                 int batch, int n_steps, int* ring, int ring_steps, int* ring_count,
+                                 b2d_stream_t stream);
+/* Replace the RoPE inverse frequencies (host, head_dim / 2 floats; default: theta^(-2i/HD) from
+ * rope_theta), e.g. with Llama-3 frequency scaling (LK/main.swift:89-108). */
+B2D_API int b2d_decoder_set_inv_freq(b2d_decoder* h, const float* inv_freq_host, int n);
 /* 1 if the steps so far use the peer-memory collectives, 0 for NCCL (or tp_size == 1). */
 B2D_API int b2d_decoder_peer_collectives(const b2d_decoder* h);
 /* Device-side status of the steps enqueued so far (synchronizes with the device): 0, or
