@@ -179,6 +179,14 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) {
   tmem_ld<16>(taddr + 16, v + 16);
 }
 
+// Weight-ring depth (stages of 64 K-columns) of the fp16 kernels.
+#ifndef B2D_TC_STAGES
+#define B2D_TC_STAGES 4
+#endif
+#ifndef B2D_TC_STAGES_DUAL
+#define B2D_TC_STAGES_DUAL 4
+#endif
+
 // QUANT: 0 = fp16 weights (TMA straight into the MMA operand), 1 = q8_32, 2 = q4_32 (TMA
 // streams the raw tiles; four dequant warps expand them into the fp16 operand).
 constexpr int threads_for(int quant) { return quant ? 192 : 128; }
@@ -192,7 +200,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
   // non-dual: 4 stages (~100 KB) so two CTAs share an SM and one streams while the other
   // runs its prologue or epilogue; dual (gate/up, 36 KB stages): one CTA per SM
-  static constexpr int STAGES = 4;
+  static constexpr int STAGES = DUAL ? B2D_TC_STAGES_DUAL : B2D_TC_STAGES;
   // quantized weights: a deep ring of RS raw tiles (the HBM stream) and a shallow ring of AS
   // operand stages [A fp16 | B] that the dequant warps fill
   static constexpr int RAW_ROW = QUANT == 1 ? BK : (QUANT == 2 ? BK / 2 : 0);  // bytes per row
