@@ -63,6 +63,7 @@ struct GemvParams {
   int M, K, nb;          // nb = tokens in this launch (<= NB)
   size_t row_bytes;      // bytes per weight row
   int n_tiles;           // row tiles
+  int kw;                // warps sharing one row group, each streaming a K slice (1, 2, 4, 8)
   // argmax
   float* logits;         // optional [nb, M]
   int ld_logits;
@@ -187,14 +188,18 @@ __device__ void stage_x(const GemvParams& p, float* xs, float* red) {
   __syncthreads();
 }
 
+#ifndef B2D_GEMV_TILES_PER_SM
+#define B2D_GEMV_TILES_PER_SM 2
+#endif
+
 template <int WT, int NB, bool DUAL>
 struct GemvCfg {
   static constexpr int R = DUAL ? 2 : (NB >= 4 ? 2 : 4);  // rows per warp
   static constexpr int U = 2;                              // chunk iterations in flight
-  static constexpr int ROWS_PER_CTA = 8 * R;
+  static constexpr int ROWS_PER_CTA = 8 * R;               // with kw = 1 (R * 8 / kw in general)
 };
 
-template <int WT, int NB, bool DUAL, bool ARGMAX>
+template <int WT, int NB, bool DUAL, bool ARGMAX, bool KSPLIT>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   using F = WFmt<WT>;
   constexpr int VEC = F::VEC;
@@ -203,12 +208,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) float xs[];  // [NB][K]
   __shared__ float red[8 * 8 * 2];
   __shared__ int redi[8 * 8];
+  // K-split partial sums of the warps of a row group: [warp][R][NB] (and the up matrix's)
+  __shared__ float kpart[8][R][NB];
+  __shared__ float kpart2[DUAL ? 8 : 1][R][NB];
 
   pdl_wait();
   stage_x<NB>(p, xs, red);
   pdl_launch_dependents();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Short, wide matrices (few row tiles, long rows) let kw warps share a row group, each
+  // streaming an interleaved slice of K, so that every SM has enough loads in flight.
+  const int kw = KSPLIT ? p.kw : 1, groups = 8 / kw, grp = warp / kw, kslice = warp % kw;
   const int K = p.K, M = p.M;
   const int nchunks = K / VEC;
   const int nscale = K / 32;
@@ -226,8 +237,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
   }
 
   for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-    const int row0 = (tile * 8 + warp) * R;
-    if (row0 >= M) continue;
+    const int row0 = (tile * groups + grp) * R;
+    const bool active = row0 < M;  // no early exit: the K-split reduce below is CTA-wide
     int rows[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) rows[r] = min(row0 + r, M - 1);
@@ -242,13 +253,13 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
         if constexpr (DUAL) acc2[r][t] = 0.f;
       }
 
-    for (int c0 = lane; c0 < nchunks; c0 += 32 * U) {
+    for (int c0 = kslice * 32 + lane; active && c0 < nchunks; c0 += 32 * U * kw) {
       uint4 wv[U][R];
       uint4 wv2[DUAL ? U : 1][R];
       float sc[U][R], sc2[DUAL ? U : 1][R];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int c = c0 + 32 * u;
+        const int c = c0 + 32 * kw * u;
         const int cc = c < nchunks ? c : c0;  // clamp: re-read a valid chunk, discarded below
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -264,7 +275,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int c = c0 + 32 * u;
+        const int c = c0 + 32 * kw * u;
         if (c >= nchunks) break;
 #pragma unroll
         for (int t = 0; t < NB; ++t) {
@@ -293,16 +304,47 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p) {
       }
     }
 
-    // reduce + epilogue
+    // reduce (warp, then across the kw warps of the group in a fixed order) + epilogue
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int t = 0; t < NB; ++t) {
+        acc[r][t] = warp_sum(acc[r][t]);
+        if constexpr (DUAL) acc2[r][t] = warp_sum(acc2[r][t]);
+      }
+    if (KSPLIT && kw > 1) {
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int t = 0; t < NB; ++t) {
+            kpart[warp][r][t] = acc[r][t];
+            if constexpr (DUAL) kpart2[warp][r][t] = acc2[r][t];
+          }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int t = 0; t < NB; ++t) {
+          float a = 0.f, a2 = 0.f;
+          for (int j = 0; j < kw; ++j) {
+            a += kpart[grp * kw + j][r][t];
+            if constexpr (DUAL) a2 += kpart2[grp * kw + j][r][t];
+          }
+          acc[r][t] = a;
+          if constexpr (DUAL) acc2[r][t] = a2;
+        }
+      __syncthreads();  // kpart is rewritten by the next tile
+    }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int row = row0 + r;
 #pragma unroll
       for (int t = 0; t < NB; ++t) {
-        float s = warp_sum(acc[r][t]);
+        const float s = acc[r][t];
         float s2 = 0.f;
-        if constexpr (DUAL) s2 = warp_sum(acc2[r][t]);
-        if (row < M && t < p.nb) {
+        if constexpr (DUAL) s2 = acc2[r][t];
+        if (active && kslice == 0 && row < M && t < p.nb) {
           if constexpr (ARGMAX) {
             if (lane == 0 && p.logits) p.logits[(size_t)t * p.ld_logits + row] = s;
             if (better(s, row, best_v[t], best_i[t])) {
@@ -393,8 +435,8 @@ struct LaunchInfo {
   int grid_cap = 0;
 };
 
-template <int WT, int NB, bool DUAL, bool ARGMAX>
-static int launch_gemv(GemvParams& p, cudaStream_t stream, int max_grid = 0) {
+template <int WT, int NB, bool DUAL, bool ARGMAX, bool KSPLIT>
+static int launch_gemv_k(GemvParams& p, cudaStream_t stream, int max_grid) {
   constexpr int ROWS = GemvCfg<WT, NB, DUAL>::ROWS_PER_CTA;
   const size_t smem = (size_t)NB * p.K * sizeof(float);
   static int cached_dev = -1;
@@ -402,7 +444,7 @@ static int launch_gemv(GemvParams& p, cudaStream_t stream, int max_grid = 0) {
   static int occ = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = gemv_kernel<WT, NB, DUAL, ARGMAX>;
+  auto kern = gemv_kernel<WT, NB, DUAL, ARGMAX, KSPLIT>;
   if (dev != cached_dev || smem != cached_smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
@@ -412,7 +454,8 @@ static int launch_gemv(GemvParams& p, cudaStream_t stream, int max_grid = 0) {
     cached_dev = dev;
     cached_smem = smem;
   }
-  p.n_tiles = (p.M + ROWS - 1) / ROWS;
+  const int rows_per_tile = ROWS / p.kw;
+  p.n_tiles = (p.M + rows_per_tile - 1) / rows_per_tile;
   int grid = std::min(p.n_tiles, std::max(1, occ) * num_sms());
   if (max_grid > 0) grid = std::min(grid, max_grid);
   cudaLaunchConfig_t cfg = {};
@@ -432,6 +475,18 @@ static int launch_gemv(GemvParams& p, cudaStream_t stream, int max_grid = 0) {
   }
   count_launch();
   return B2D_OK;
+}
+
+// kw: the fewest warps per row group that still give every SM B2D_GEMV_TILES_PER_SM row tiles;
+// matrices with enough rows keep the plain kernel (one warp per row group).
+template <int WT, int NB, bool DUAL, bool ARGMAX>
+static int launch_gemv(GemvParams& p, cudaStream_t stream, int max_grid = 0) {
+  constexpr int ROWS = GemvCfg<WT, NB, DUAL>::ROWS_PER_CTA;
+  p.kw = 1;
+  while (p.kw < 8 && (p.M + ROWS / p.kw - 1) / (ROWS / p.kw) < B2D_GEMV_TILES_PER_SM * num_sms())
+    p.kw *= 2;
+  return p.kw > 1 ? launch_gemv_k<WT, NB, DUAL, ARGMAX, true>(p, stream, max_grid)
+                  : launch_gemv_k<WT, NB, DUAL, ARGMAX, false>(p, stream, max_grid);
 }
 
 // Largest fp32 activation staging per CTA (bytes): NB * K * 4 must fit.
