@@ -185,3 +185,18 @@ def test_large_batch_many_short_sequences():
     ro, rk, rv = run_oracle(c, 32, 8, 64, 500000.0)
     assert_rel_close(go, ro, 2e-3)
     check_pages(gk, gv, rk, rv)
+
+
+def test_long_chunks_of_1024_keys():
+    """40 sequences of 2000-3500 tokens: the chunk heuristic picks 1024-key chunks (the largest),
+    so each CTA's page list is the longest the kernel supports."""
+    from gemmagemini4hackathon2026_10_2425_b200 import _lib
+
+    r = np.random.default_rng(1024)
+    lens = r.integers(2000, 3500, size=40).tolist()
+    assert _lib.lib().b2d_attn_chunk_tokens(40, 8, max(lens) + 1) == 1024
+    c = make_case(lens, 32, 8, 64, seed=1025, extra_blocks=3)
+    go, gk, gv = run_gpu(c, 32, 8, 64, 500000.0)
+    ro, rk, rv = run_oracle(c, 32, 8, 64, 500000.0)
+    assert_rel_close(go, ro, 2e-3)
+    check_pages(gk, gv, rk, rv)
