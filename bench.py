@@ -291,9 +291,16 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
         x = torch.randn(1, K, generator=g, device=dev)
         gm = 1 + 0.1 * torch.randn(K, generator=g, device=dev)
         y = torch.empty(1, M, device=dev)
-        ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), nit(50 if M > 100000 else 200), s)
         b = M * K * 2 + K * 4 + K * 4 + M * 4
+        its = nit(50 if M > 100000 else 200)
+        ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), its, s)
         res[f"c2_f16_{K}to{M}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+        prev = ops.gemv_mma_formats(ops.gemv_mma_formats() - {"f16"})  # the CUDA-core GEMV, for comparison
+        try:
+            ms = time_launches(lambda i: ops.gemv(Ws[i % n], x, gamma=gm, eps=1e-6, y=y), its, s)
+        finally:
+            ops.gemv_mma_formats(prev)
+        res[f"c2_f16_{K}to{M}_cuda_cores"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
         del Ws
     # config 3: q8 / q4, batch 1 and 16
     for fmt in ("q8", "q4"):
@@ -315,13 +322,23 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
                     continue
                 x = torch.randn(bsz, K, generator=g, device=dev).half()
                 y = torch.empty(bsz, M, device=dev)
-                if bsz >= 9:  # tensor-core path: raw tiles dequantized in shared memory
+                b = wbytes + bsz * K * 2 + bsz * M * 4
+                key = f"c3_{fmt}_{K}to{M}_b{bsz}"
+                # b2d_gemv: the tensor-core GEMV (integer weights as exact fp16 on mma.sync)
+                ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
+                res[key] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+                # the alternatives it replaced, for comparison: CUDA cores, and at batch 16 the
+                # tcgen05 GEMM with the raw tiles dequantized in shared memory
+                prev = ops.gemv_mma_formats(ops.gemv_mma_formats() - {fmt})
+                try:
+                    ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
+                finally:
+                    ops.gemv_mma_formats(prev)
+                res[key + "_cuda_cores"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+                if bsz >= 9:
                     wsq = torch.zeros(ops.tc_workspace_bytes(M, K, bsz), dtype=torch.uint8, device=dev)
                     ms = time_launches(lambda i: ops.gemm_tc_q(Wq[i % n], x, y=y, workspace=wsq), nit(100), s)
-                else:
-                    ms = time_launches(lambda i: ops.gemv(Wq[i % n], x, y=y), nit(100), s)
-                b = wbytes + bsz * K * 2 + bsz * M * 4
-                res[f"c3_{fmt}_{K}to{M}_b{bsz}"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
+                    res[key + "_tcgen05"] = {"us": ms * 1e3, "gbs": b / ms / 1e6, "frac": b / ms / 1e6 / peak}
             del Wq
     # config 5 building blocks at batch 32: the tcgen05 projections (weights rotated over 16
     # layer copies so every launch streams from HBM) and the HD-64 paged attention
@@ -469,16 +486,26 @@ def run_ours(args) -> None:
         return float(t.item())
 
     # ---- device-resident loop: same inputs every step (fixed contexts), graph replay
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(s):
+        w0.record(s)
         for _ in range(args.warmup):
             eng.step(tok_d, ctx_d, table, nxt_d)
+        w1.record(s)
     n0 = _lib.lib().b2d_launch_counter()
     torch.cuda.synchronize()
+    # untimed steps enqueued right before the timed ones (~0.3 s of work, no idle gap between
+    # them): the timed region starts from a busy GPU, not from the sampler's start-up pause
+    n_pre = min(2000, max(args.warmup, int(300.0 / max(w0.elapsed_time(w1) / args.warmup, 1e-3))))
+    n_pre = int(max_over_ranks(float(n_pre)))  # every rank runs the same steps
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         time.sleep(0.3)
+        with torch.cuda.stream(s):
+            for _ in range(n_pre):
+                eng.step(tok_d, ctx_d, table, nxt_d)
         e0.record(s)
         for _ in range(args.steps):
             eng.step(tok_d, ctx_d, table, nxt_d)

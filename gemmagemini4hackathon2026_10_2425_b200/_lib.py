@@ -53,6 +53,7 @@ SIGNATURES = {
     "b2d_launch_counter": (C.c_longlong, []),
     "b2d_gemv_f32": (I, [P, P, P, I, I, P]),
     "b2d_gemv": (I, [I, P, P, P, P, I, P, I, P, Fl, I, I, P, I, P, I, I, I, P]),
+    "b2d_gemv_mma_formats": (I, [I]),
     "b2d_rmsnorm_gemv_f16": (I, [P, P, P, Fl, P, I, I, I, I, P, P, P]),
     "b2d_gemv_q8_32": (I, [P, P, P, P, I, I, I, P]),
     "b2d_gemv_q4_32": (I, [P, P, P, P, I, I, I, P]),

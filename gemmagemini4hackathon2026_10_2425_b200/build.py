@@ -24,7 +24,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libb200dec.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["capi.cu", "gemv.cu", "ops.cu", "attention.cu", "decoder.cu", "noalloc.cu", "tc_gemm.cu", "tp_peer.cu"]
+SOURCES = ["capi.cu", "gemv.cu", "gemv_mma.cu", "ops.cu", "attention.cu", "decoder.cu", "noalloc.cu", "tc_gemm.cu", "tp_peer.cu"]
 
 
 def nvcc() -> str:

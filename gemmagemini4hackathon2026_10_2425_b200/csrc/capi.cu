@@ -25,7 +25,8 @@ int num_sms() {
   return cached[dev];
 }
 
-// implemented in gemv.cu / ops.cu / attention.cu
+// implemented in gemv.cu / gemv_mma.cu / ops.cu / attention.cu
+int gemv_mma_formats(int mask);
 int gemv_dispatch(int, const void*, const void*, const void*, const void*, int, const void*, int,
                   const float*, float, int, int, void*, int, const float*, int, int, int,
                   cudaStream_t);
@@ -96,6 +97,8 @@ int b2d_gemv_f32(const float* W, const float* x, float* y, int M, int K, b2d_str
   return gemv_dispatch(B2D_F32, W, nullptr, nullptr, nullptr, B2D_F32, x, K, nullptr, 0.f,
                        B2D_EPI_STORE, B2D_F32, y, M, nullptr, M, K, 1, S(stream));
 }
+
+int b2d_gemv_mma_formats(int mask) { return gemv_mma_formats(mask); }
 
 int b2d_gemv(int w_dtype, const void* W, const void* W_scales, const void* W_up,
              const void* W_up_scales, int x_dtype, const void* x, int ldx, const float* gamma,

@@ -526,6 +526,14 @@ static int run_groups(GemvParams p, int batch, cudaStream_t stream) {
   return B2D_OK;
 }
 
+// Tensor-core GEMV for quantized (and optionally fp16) weights, gemv_mma.cu.
+bool gemv_mma_eligible(int w_dtype, const void* W_scales, const void* W_up_scales, int K,
+                       int epilogue);
+int gemv_mma_dispatch(int w_dtype, const void* W, const void* W_scales, const void* W_up,
+                      const void* W_up_scales, int x_dtype, const void* x, int ldx,
+                      const float* gamma, float eps, int epilogue, int y_dtype, void* y, int ldy,
+                      const float* aux, int M, int K, int batch, cudaStream_t stream);
+
 static size_t elem_row_bytes(int w_dtype, int K) {
   switch (w_dtype) {
     case B2D_F32: return (size_t)K * 4;
@@ -558,6 +566,9 @@ int gemv_dispatch(int w_dtype, const void* W, const void* W_scales, const void* 
   const size_t xsz = x_dtype == B2D_F16 ? 2 : 4;
   if (!aligned16(W) || !aligned16(x) || ((size_t)ldx * xsz) % 16 || (W_up && !aligned16(W_up)))
     return B2D_ERR_ALIGN;
+  if (gemv_mma_eligible(w_dtype, W_scales, W_up_scales, K, epilogue))
+    return gemv_mma_dispatch(w_dtype, W, W_scales, W_up, W_up_scales, x_dtype, x, ldx, gamma, eps,
+                             epilogue, y_dtype, y, ldy, aux, M, K, batch, stream);
   GemvParams p = {};
   p.W = W;
   p.Ws = static_cast<const uint16_t*>(W_scales);

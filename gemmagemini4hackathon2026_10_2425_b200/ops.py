@@ -151,6 +151,18 @@ def gemv(
     return y2[0] if squeeze and y.dim() == 1 else y
 
 
+_MMA_FMT = {"f16": _lib.F16, "q8": _lib.Q8_32, "q4": _lib.Q4_32, "int8_b1": 4}
+
+
+def gemv_mma_formats(formats: set[str] | None = None) -> set[str]:
+    """Weight formats ('f16', 'q8', 'q4') that gemv() runs on the tensor-core GEMV, plus
+    'int8_b1' (a quantized single token on the integer tensor cores); `formats` replaces the set
+    (process-wide).  Returns the previous set."""
+    mask = -1 if formats is None else sum(1 << _MMA_FMT[f] for f in formats)
+    prev = _lib.lib().b2d_gemv_mma_formats(mask)
+    return {f for f, d in _MMA_FMT.items() if (prev >> d) & 1}
+
+
 def gemv_f32(W: torch.Tensor, x: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
     """Config 1: fp32 y = W @ x (x [K])."""
     M, K = W.shape

@@ -96,7 +96,20 @@ B2D_API int b2d_gemv_f32(const float* W, const float* x, float* y, int M, int K,
  *             LK/kernels.metal:144-173).
  * x_dtype is F32 or F16.  K must be a multiple of 32 for Q*, 8 for F16, 4 for F32.
  * batch >= 1 (rows are processed in groups; batch <= 8 streams W once).
- * ARGMAX is served by b2d_lm_head_argmax. */
+ * ARGMAX is served by b2d_lm_head_argmax.
+ * F16, Q8_32 and Q4_32 weights (the formats enabled with b2d_gemv_mma_formats) whose row is a
+ * multiple of 128 bytes, with scales 8-byte (Q8) / 16-byte (Q4) aligned, run on the tensor-core
+ * GEMV: weights as exact fp16 on mma.sync (integers dequantized exactly), the block scale
+ * applied to each block's fp32 result, up to 16 fp16 tokens (8 when x is fp32 or normalized:
+ * hi + lo fp16 columns) per pass over W.  Everything else (F32 weights) runs on CUDA cores. */
+/* Weight dtypes that b2d_gemv sends to the tensor-core GEMV: bit d set for dtype d (F16, Q8_32,
+ * Q4_32; F32 is ignored); bit 4 (B2D_GEMV_MMA_INT8_B1): a quantized GEMV of one token runs on the
+ * integer tensor cores (the token as 3 int8 digits of a 21-bit fixed-point value, exact int32
+ * block sums).  Default (1 << B2D_F16) | (1 << B2D_Q8_32) | (1 << B2D_Q4_32).  mask < 0 only
+ * queries.  Returns the previous mask.  Process-wide; set it before capturing graphs. */
+#define B2D_GEMV_MMA_INT8_B1 16
+B2D_API int b2d_gemv_mma_formats(int mask);
+
 B2D_API int b2d_gemv(int w_dtype, const void* W, const void* W_scales, const void* W_up,
              const void* W_up_scales, int x_dtype, const void* x, int ldx, const float* gamma,
              float eps, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,

@@ -61,17 +61,19 @@ def synth_weights(cfg: ModelConfig, seed: int, std: float = 0.02) -> dict[str, n
     return w
 
 
-def _layer_attention(cfg, qkv, k_pages, v_pages, block_table, ctx_lens, invf, n_heads, n_kv):
+def _layer_attention(cfg, qkv, k_pages, v_pages, block_table, ctx_lens, invf, n_heads, n_kv, append=True):
     return ops.paged_decode_attention(
-        qkv, k_pages, v_pages, block_table, ctx_lens, n_heads, n_kv, cfg.head_dim, invf
+        qkv, k_pages, v_pages, block_table, ctx_lens, n_heads, n_kv, cfg.head_dim, invf, append=append
     )
 
 
-def decode_step(w, cfg: ModelConfig, tokens, ctx_lens, block_table, k_pages, v_pages):
+def decode_step(w, cfg: ModelConfig, tokens, ctx_lens, block_table, k_pages, v_pages, append=True):
     """One decode step for B sequences.  Returns (logits [B, V] float64, next tokens [B]).
 
     tokens[b] is the token at position ctx_lens[b]; k_pages/v_pages are per-layer lists of
-    [n_blocks, Hkv, 16, HD] arrays, updated in place with the new token's K/V.
+    [n_blocks, Hkv, 16, HD] arrays, updated in place with the new token's K/V.  With
+    append=False the pages must already hold the new token's (rotated, fp16) K/V -- e.g. the
+    pages a GPU step wrote -- and are only read, so the step is evaluated over exactly that cache.
       x = embed(tokens)                                          LK/main.swift:323-330
       per layer:                                                 LK/main.swift:332-341
         qkv = rmsnorm(x, attn_norm) @ wqkv^T
@@ -85,7 +87,7 @@ def decode_step(w, cfg: ModelConfig, tokens, ctx_lens, block_table, k_pages, v_p
     for i in range(cfg.n_layers):
         qkv = ops.gemv(w[f"l{i}.wqkv"], ops.rmsnorm(x, w[f"l{i}.attn_norm"], cfg.eps))
         att = _layer_attention(
-            cfg, qkv, k_pages[i], v_pages[i], block_table, ctx_lens, invf, cfg.n_heads, cfg.n_kv_heads
+            cfg, qkv, k_pages[i], v_pages[i], block_table, ctx_lens, invf, cfg.n_heads, cfg.n_kv_heads, append
         )
         x = x + ops.gemv(w[f"l{i}.wo"], att)
         xn = ops.rmsnorm(x, w[f"l{i}.ffn_norm"], cfg.eps)
