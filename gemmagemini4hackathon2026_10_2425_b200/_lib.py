@@ -96,6 +96,7 @@ SIGNATURES = {
     "b2d_decoder_step": (I, [P, P, P, P, I, P, P, I, P]),
     "b2d_decoder_peer_collectives": (I, [P]),
     "b2d_decoder_generate": (I, [P, P, P, P, I, I, P, I, P, P]),
+    "b2d_decoder_prefill": (I, [P, P, I, P, I, P, P, P]),
     "b2d_decoder_set_inv_freq": (I, [P, P, I]),
     "b2d_decoder_error": (I, [P]),
     "b2d_tp_allreduce_add_rmsnorm": (I, [P, P, P, I, I, I, P, P, Fl, P, I, I, C.c_longlong, P, P]),

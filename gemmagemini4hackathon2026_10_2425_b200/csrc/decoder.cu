@@ -43,6 +43,8 @@ size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
                       void*, size_t, cudaStream_t);
+int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
+                   const float*, int, int, int, int, cudaStream_t);
 int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, int, int, cudaStream_t);
 int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*, int,
                       int, cudaStream_t);
@@ -134,7 +136,10 @@ struct b2d_decoder {
   cudaGraphExec_t gexec = nullptr;
   GraphKey gkey;
   // device-resident decode loop (b2d_decoder_generate): step + advance, captured once
-  int* gen_next = nullptr;  // [B] next tokens of the loop's step
+  int* gen_next = nullptr;  // [B] next tokens of the loop's step (also prefill's last chunk)
+  // chunked prefill: positions [2][B] and block-table rows [2][B][max_blocks] of a chunk
+  int* pf_ctx = nullptr;
+  int* pf_table = nullptr;
   cudaGraphExec_t gen_exec = nullptr;
   GraphKey gen_key;
 };
@@ -195,11 +200,31 @@ static int tp_argmax(b2d_decoder* h, int B, int* next_tokens, cudaStream_t s) {
   return argmax_combine(h->cand_val, h->cand_idx, h->tp, B, next_tokens, s);
 }
 
+// RoPE + KV append and attention of one layer.  In a decode step each token's K/V is appended by
+// the attention kernel itself.  In a prefill chunk the tokens are consecutive positions of one
+// sequence and each attends to the ones before it, so the whole chunk's K/V is written first
+// (rope_kv_append, a plain launch: it starts after the QKV projection has completed) and the
+// attention then only reads the pages.
+static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
+                           const int* block_table, int B, bool prefill, void* out, int out_dtype,
+                           cudaStream_t s) {
+  const b2d_model_config& c = h->cfg;
+  const int HD = c.head_dim;
+  if (prefill)
+    B2D_TRY(rope_kv_append(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
+                           c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B, s));
+  return paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
+                           c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
+                           c.max_ctx, 0.f, 0, prefill ? 0 : 1, out, out_dtype, h->hq * HD,
+                           h->attn_ws, h->attn_ws_bytes, s);
+}
+
 // Tensor-core step (batch >= kTcMinBatch): activations enter each projection as fp16
 // (RMSNorm fused into the producer of the operand), weights are read once per step.
+// next_tokens == nullptr skips the LM head (a prefill chunk whose outputs nobody reads).
 static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                            const int* block_table, int B, int* next_tokens, float* logits,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool prefill) {
   const b2d_model_config& c = h->cfg;
   const int D = c.dim, HD = c.head_dim, HQD = h->hq * c.head_dim;
   const bool tpar = h->tp > 1;
@@ -214,10 +239,7 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     B2D_TRY(tc_gemm(L.wqkv, nullptr, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
                     nullptr, h->qkv_l, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
     // RoPE + KV append + split-K attention -> fp16 operand of the O projection
-    B2D_TRY(paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
-                              c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
-                              c.max_ctx, 0.f, 0, 1, h->att16, B2D_F16, HQD, h->attn_ws,
-                              h->attn_ws_bytes, s));
+    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, B2D_F16, s));
     // O projection (row-parallel) + residual, then RMSNorm(ffn) -> fp16
     if (!tpar) {
       B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
@@ -241,6 +263,7 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     }
   }
   // LM head (vocab-parallel) + argmax
+  if (!next_tokens) return B2D_OK;
   const int offset = h->rank * h->lm_stride;
   if (!tpar) {
     B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
@@ -252,6 +275,17 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
   return B2D_OK;
+}
+
+// A prefill chunk's per-row inputs: row b is position pos0 + b of the sequence whose block-table
+// row is seq_table (every row of the chunk reads and writes the same pages).
+__global__ void prefill_chunk_kernel(const int* seq_table, int max_blocks, int pos0, int nb,
+                                     int* ctx, int* table) {
+  const int b = blockIdx.x;
+  if (b >= nb) return;
+  if (threadIdx.x == 0) ctx[b] = pos0 + b;
+  for (int j = threadIdx.x; j < max_blocks; j += blockDim.x)
+    table[(size_t)b * max_blocks + j] = seq_table[j];
 }
 
 // Device-resident loop: after a step, the next tokens become the inputs of the following step,
@@ -272,9 +306,9 @@ __global__ void advance_kernel(int* tokens, int* ctx_lens, const int* next, int*
 // Enqueue one decode step on `s` (no synchronization, graph-capturable).
 static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                         const int* block_table, int B, int* next_tokens, float* logits,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool prefill = false) {
   if (B >= kTcMinBatch)
-    return enqueue_step_tc(h, tokens, ctx_lens, block_table, B, next_tokens, logits, s);
+    return enqueue_step_tc(h, tokens, ctx_lens, block_table, B, next_tokens, logits, s, prefill);
   const b2d_model_config& c = h->cfg;
   const int D = c.dim, HD = c.head_dim;
   const bool tpar = h->tp > 1;
@@ -286,10 +320,7 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                           L.attn_norm, c.eps, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l, nullptr,
                           h->qkv_l, D, B, s));
     // RoPE + KV append + split-K GQA attention over the paged cache
-    B2D_TRY(paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
-                              c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
-                              c.max_ctx, 0.f, 0, 1, h->att, B2D_F32, h->hq * HD, h->attn_ws,
-                              h->attn_ws_bytes, s));
+    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att, B2D_F32, s));
     // O projection (row-parallel) + residual
     if (!tpar) {
       B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
@@ -318,6 +349,7 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
     }
   }
   // final RMSNorm + LM head (vocab-parallel) + argmax
+  if (!next_tokens) return B2D_OK;
   const int offset = h->rank * h->lm_stride;  // first vocab row of this rank
   if (!tpar) {
     B2D_TRY(lm_head_argmax(h->lm_head, h->x, D, h->final_norm, c.eps, h->lm_rows, D, B, 0,
@@ -469,6 +501,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
       (size_t)B * D * 4,          (size_t)B * h->qkv_l * 4, (size_t)B * h->hq * c.head_dim * 4,
       (size_t)B * h->fl * 4,      (size_t)(B + 1) * 4,      (size_t)c.head_dim / 2 * 4,
       (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)4,  (size_t)B * 4,
+      (size_t)2 * B * 4,          (size_t)2 * B * c.max_blocks * 4,
       h->attn_ws_bytes,           h->am_ws_bytes,
       (size_t)B * D * 2,          (size_t)B * h->hq * c.head_dim * 2, (size_t)B * h->fl * 2,
       h->tc_ws_bytes};
@@ -485,6 +518,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
                     (void**)&h->hid,      (void**)&h->epochs,   (void**)&h->invf,
                     (void**)&h->cand_val, (void**)&h->cand_idx, (void**)&h->err,
                     (void**)&h->gen_next,
+                    (void**)&h->pf_ctx,   (void**)&h->pf_table,
                     (void**)&h->attn_ws,  (void**)&h->am_ws,
                     (void**)&h->xn16,     (void**)&h->att16,    (void**)&h->h16,
                     (void**)&h->tc_ws};
@@ -631,6 +665,41 @@ int b2d_decoder_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
     h->gkey = key;
   }
   return cuda_status(cudaGraphLaunch(h->gexec, s));
+}
+
+int b2d_decoder_prefill(b2d_decoder* h, const int* tokens, int n, const int* seq_table,
+                        int start_pos, int* next_token, float* logits, b2d_stream_t stream) {
+  if (!h) return B2D_ERR_NULL;
+  if (!tokens || !seq_table || !next_token) return B2D_ERR_NULL;
+  if (n <= 0 || start_pos < 0 || start_pos + n > h->cfg.max_ctx) return B2D_ERR_SHAPE;
+  if (!h->embed) return B2D_ERR_STATE;
+  for (const Layer& L : h->layers)
+    if (!L.wqkv) return B2D_ERR_STATE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int chunk = h->cfg.max_batch, mb = h->cfg.max_blocks;
+  // with logits, the last token runs as its own step (its logits row is the caller's buffer)
+  const int n_chunked = logits ? n - 1 : n;
+  int parity = 0;
+  auto run = [&](int c0, int nb, bool last_out, float* lg) -> int {
+    int* ctx = h->pf_ctx + (size_t)parity * chunk;
+    int* table = h->pf_table + (size_t)parity * chunk * mb;
+    parity ^= 1;  // the previous chunk's kernels may still read the other pair
+    prefill_chunk_kernel<<<nb, 128, 0, s>>>(seq_table, mb, start_pos + c0, nb, ctx, table);
+    B2D_TRY(launch_status());
+    return enqueue_step(h, tokens + c0, ctx, table, nb, last_out ? h->gen_next : nullptr, lg, s,
+                        true);
+  };
+  for (int c0 = 0; c0 < n_chunked; c0 += chunk) {
+    const int nb = std::min(chunk, n_chunked - c0);
+    const bool last = !logits && c0 + nb == n;
+    B2D_TRY(run(c0, nb, last, nullptr));
+    if (last)
+      return cuda_status(cudaMemcpyAsync(next_token, h->gen_next + nb - 1, sizeof(int),
+                                         cudaMemcpyDeviceToDevice, s));
+  }
+  B2D_TRY(run(n - 1, 1, true, logits));
+  return cuda_status(
+      cudaMemcpyAsync(next_token, h->gen_next, sizeof(int), cudaMemcpyDeviceToDevice, s));
 }
 
 int b2d_decoder_generate(b2d_decoder* h, int* tokens, int* ctx_lens, const int* block_table,

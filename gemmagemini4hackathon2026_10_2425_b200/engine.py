@@ -277,6 +277,42 @@ class DecodeEngine:
         )
         return ring
 
+    def prefill(
+        self,
+        tokens: torch.Tensor,
+        seq_table: torch.Tensor,
+        start_pos: int = 0,
+        next_token: torch.Tensor | None = None,
+        logits: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        """Enqueue the prefill of one sequence (no host sync): tokens int32 [n] (device) at
+        positions start_pos .. start_pos + n - 1, K/V written into the pages of seq_table
+        (int32 [max_blocks], device), in chunks of max_batch positions per step.  Returns
+        next_token (int32 [1]): the greedy token after the last one; logits (fp32 [lm_rows])
+        receives the last position's logits if given."""
+        n = tokens.numel()
+        for t in (tokens, seq_table):
+            if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("tokens, seq_table: contiguous CUDA int32")
+        if seq_table.numel() != self.max_blocks:
+            raise ValueError(f"seq_table must hold {self.max_blocks} block ids")
+        if next_token is None:
+            next_token = torch.empty(1, dtype=torch.int32, device=tokens.device)
+        if logits is not None and (logits.dtype != torch.float32 or logits.numel() < self.lm_rows):
+            raise ValueError(f"logits must be fp32 with >= {self.lm_rows} elements")
+        call(
+            "b2d_decoder_prefill",
+            self._h,
+            tokens.data_ptr(),
+            n,
+            seq_table.data_ptr(),
+            start_pos,
+            next_token.data_ptr(),
+            None if logits is None else logits.data_ptr(),
+            self.stream.cuda_stream,
+        )
+        return next_token
+
     def peer_collectives(self) -> bool:
         """True if the tensor-parallel sums run over NVLink peer memory (False: NCCL or tp 1)."""
         return bool(_lib.lib().b2d_decoder_peer_collectives(self._h))

@@ -18,9 +18,10 @@ This module is that binary for the CUDA path; `kernel_folder/llm` runs its main(
         "prefill_s", "decode_s"}
     -> {"error": "..."} for a bad request (the process keeps serving); EOF on stdin ends it.
 
-One sequence at a time (batch 1), greedy, every request from an empty cache.  The prompt is run
-through the decode step one token per step (the reference's --no-gemm prefill); a GEMM prefill
-is not part of this path.
+One sequence at a time (batch 1), greedy, every request from an empty cache.  The prompt is
+prefilled in chunks of 32 consecutive positions per step (b2d_decoder_prefill: tcgen05
+projections, each chunk's K/V written before its rows attend); --no-gemm prefills one token per
+decode step, as the reference's --no-gemm does.
 """
 
 from __future__ import annotations
@@ -47,7 +48,7 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--kernels", default=None, help="ignored (Metal source path in the reference)")
     ap.add_argument("--define", action="append", default=[], help="ignored (Metal defines in the reference)")
-    ap.add_argument("--no-gemm", action="store_true", help="ignored: the prompt always runs through decode steps")
+    ap.add_argument("--no-gemm", action="store_true", help="prefill one token per decode step instead of 32-position chunks")
     return ap.parse_args(argv)
 
 
@@ -71,11 +72,14 @@ def parse_request(line: str, vocab: int, max_ctx: int) -> tuple[list[int], int, 
     return ids, max_tokens, stop
 
 
+PREFILL_CHUNK = 32  # positions per prefill step (the tcgen05 projections take up to 32 rows)
+
+
 class Session:
     """One sequence on one GPU: the weights file in a DecodeEngine, a contiguous block table,
     and a captured decode step fed through pinned host buffers."""
 
-    def __init__(self, weights: str, max_ctx: int):
+    def __init__(self, weights: str, max_ctx: int, chunked_prefill: bool = True):
         import torch
 
         from . import weights as W
@@ -87,7 +91,9 @@ class Session:
         self.max_ctx = max_ctx
         blocks = -(-max_ctx // 16)
         dev = torch.device("cuda", torch.cuda.current_device())
-        self.eng = DecodeEngine(self.shape, max_batch=1, max_ctx=max_ctx, n_blocks=blocks, device=dev)
+        self.chunked = chunked_prefill
+        batch = PREFILL_CHUNK if chunked_prefill else 1
+        self.eng = DecodeEngine(self.shape, max_batch=batch, max_ctx=max_ctx, n_blocks=blocks, device=dev)
         self.eng.alloc_kv()
         self.eng.load_weights_file(weights)
         self.table = torch.arange(blocks, dtype=torch.int32, device=dev).view(1, blocks)
@@ -114,12 +120,24 @@ class Session:
         s.synchronize()
         return int(self.h_out[0])
 
-    def prefill(self, ids: list[int]) -> int:
-        """Run the prompt (positions 0..n-1) and return the first generated token."""
-        nxt = 0
-        for p, t in enumerate(ids):
-            nxt = self.step(t, p)
-        return nxt
+    def prefill(self, ids: list[int], want_logits: bool = False) -> int:
+        """Run the prompt (positions 0..n-1) and return the first generated token; with
+        want_logits, last_logits() then holds the last position's logits."""
+        if not self.chunked:
+            nxt = 0
+            for p, t in enumerate(ids):
+                nxt = self.step(t, p)
+            return nxt
+        torch = self.torch
+        s = self.eng.stream
+        ids_h = torch.tensor(ids, dtype=torch.int32).pin_memory()
+        with torch.cuda.stream(s):
+            ids_d = ids_h.to(self.tok.device, non_blocking=True)
+            self.eng.prefill(ids_d, self.table[0], 0, next_token=self.nxt,
+                             logits=self.logits[0] if want_logits else None)
+            self.h_out.copy_(self.nxt, non_blocking=True)
+        s.synchronize()
+        return int(self.h_out[0])
 
     def last_logits(self):
         return self.logits[0].float().cpu().numpy()
@@ -176,15 +194,15 @@ def _stats(xs: list[float]) -> tuple[float, float]:
 
 def main(argv=None) -> int:
     a = parse_args(argv)
-    sess = Session(a.weights, a.max_ctx)
+    sess = Session(a.weights, a.max_ctx, chunked_prefill=not a.no_gemm)
     s = sess.shape
-    print(f"device: {sess.device_name}, dim {s.dim}, layers {s.n_layers}, vocab {s.vocab}, gemm false", file=sys.stderr)
+    print(f"device: {sess.device_name}, dim {s.dim}, layers {s.n_layers}, vocab {s.vocab}, gemm {str(sess.chunked).lower()}", file=sys.stderr)
     if a.prompt_ids:
         ids = [int(t) for t in a.prompt_ids.split(",")]
         if len(ids) + a.gen > a.max_ctx:
             raise SystemExit("prompt + gen exceeds --max-ctx")
         t0 = time.perf_counter()
-        tok = sess.prefill(ids)
+        tok = sess.prefill(ids, want_logits=bool(a.dump_logits))
         t_prefill = time.perf_counter() - t0
         if a.dump_logits:
             sess.last_logits().astype("<f4").tofile(a.dump_logits)
@@ -200,7 +218,7 @@ def main(argv=None) -> int:
             "decode_tok_s": (a.gen - 1) / t_dec if a.gen > 1 and t_dec > 0 else 0,
         }))
     if a.bench_pp > 0 or a.bench_tg > 0:
-        report = {"tunables": {"prefill": "decode steps", "batch": 1, "graph": True}}
+        report = {"tunables": {"prefill": f"chunks of {PREFILL_CHUNK}" if sess.chunked else "decode steps", "batch": 1, "graph": True}}
         if a.bench_pp > 0:
             n = min(a.bench_pp, a.max_ctx - 1)
             ids = [(i * 7919 % 100000 + 1000) % s.vocab for i in range(n)]

@@ -320,6 +320,18 @@ B2D_API int b2d_nccl_get_unique_id(void* out_host);
 B2D_API int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
                        const void* nccl_id, b2d_decoder** out);
 B2D_API int b2d_decoder_destroy(b2d_decoder* h);
+/* Prefill: run the n prompt tokens (device array) of one sequence at positions start_pos ..
+ * start_pos + n - 1 through the model, writing their K/V into the pages of the sequence's
+ * block-table row seq_table [max_blocks] (device), and set next_token (device int) to the greedy
+ * token after the last one; logits (device [lm_rows], optional) receives the last position's
+ * logits.  The tokens go through the decode step in chunks of max_batch consecutive positions
+ * (LK/main.swift:357-372 prefills in chunks of rows too): each chunk's K/V is written first,
+ * then every row attends to the positions up to its own, so a chunk costs one step (tcgen05
+ * projections from 9 rows up) instead of one step per token.  Not graph-captured; collective
+ * across tensor-parallel ranks (every rank calls it with the same arguments). */
+B2D_API int b2d_decoder_prefill(b2d_decoder* h, const int* tokens, int n, const int* seq_table,
+                                int start_pos, int* next_token, float* logits, b2d_stream_t stream);
+
 /* Device-resident greedy decode loop: n_steps decode steps back to back with no host round trip.
  * After each step the next tokens replace tokens[b], ctx_lens[b] grows by one, and the tokens
  * are written to ring row (*ring_count % ring_steps), ring [ring_steps][batch] int32, after which
