@@ -789,13 +789,18 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
 // more CTAs than SMs and without splitting K below one 64-wide tile.
 template <int N, bool DUAL, int QUANT = 0>
 static int tc_pick_splits(int m_tiles, int k_tiles) {
-  // The largest power-of-two split (<= 8, the portable cluster size) whose CTAs still fit on the
-  // SMs (<= one CTA per SM: no cluster waits for a second wave).  An earlier rule that
+  // The largest power-of-two split (<= 8, the portable cluster size) whose CTAs all fit on the
+  // SMs at once: two per SM for the single-matrix fp16 kernel (about 100 KB of shared memory;
+  // QKV 6.9 -> 6.3 us with 8-way splits), one for the others.  An earlier rule that
   // also asked cudaOccupancyMaxActiveClusters for a full wave of clusters picked 4-way splits
   // for the down and O projections (64 CTAs on 148 SMs): 14.6 -> 10.3 us and 7.5 -> 6.1 us
   // measured on B200 with the split that fills the SMs.
+#ifndef B2D_TC_SPLIT_CTAS_PER_SM
+#define B2D_TC_SPLIT_CTAS_PER_SM 2
+#endif
+  const int slots = (!DUAL && !QUANT ? B2D_TC_SPLIT_CTAS_PER_SM : 1) * num_sms();
   for (int ks = 8; ks >= 2; ks >>= 1)
-    if (ks <= k_tiles && m_tiles * ks <= num_sms()) return ks;
+    if (ks <= k_tiles && m_tiles * ks <= slots) return ks;
   return 1;
 }
 
