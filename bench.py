@@ -38,7 +38,7 @@ FALLBACK_HBM = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # DRAM bytes per launch from one ncu capture of each kernel (dram__bytes_read.sum +
 # dram__bytes_write.sum); commands and figures in profiles/paged_attn_c5_hd64.md and
 # profiles/tc_gemm_gateup_c5.md
-ATTN_C5_TRAFFIC = 160_088_832 + 4_641_024
+ATTN_C5_TRAFFIC = 160_088_832 + 3_824_384
 GATEUP_TRAFFIC = 67_329_280 + 683_264
 
 
