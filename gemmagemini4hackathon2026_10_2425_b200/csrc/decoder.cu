@@ -226,7 +226,7 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                            const int* block_table, int B, int* next_tokens, float* logits,
                            cudaStream_t s, bool prefill) {
   const b2d_model_config& c = h->cfg;
-  const int D = c.dim, HD = c.head_dim, HQD = h->hq * c.head_dim;
+  const int D = c.dim, HQD = h->hq * c.head_dim;
   const bool tpar = h->tp > 1;
   void* ws = h->tc_ws;
   const size_t wsb = h->tc_ws_bytes;
