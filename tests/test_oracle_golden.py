@@ -121,6 +121,23 @@ def test_decode_step_tp_equals_single(golden):
                 np.testing.assert_array_equal(a, b)
 
 
+def test_decode_step_over_written_cache(golden):
+    """append=False (the mode the GPU tests use to evaluate the oracle over the cache a GPU step
+    wrote): over pages that already hold the new tokens' K/V it reproduces the appending step
+    exactly and writes nothing."""
+    cfg = _tiny_cfg(golden)
+    w = _tiny_weights(golden, cfg)
+    lens, table, kp, vp = build_paged_cache(golden, cfg, np.float16)
+    tokens = [int(golden[f"llm_s{b}_ids"][-1]) for b in range(len(lens))]
+    l1, n1 = step.decode_step(w, cfg, tokens, lens, table, kp, vp)  # appends into kp / vp
+    kp2, vp2 = [k.copy() for k in kp], [v.copy() for v in vp]
+    l2, n2 = step.decode_step(w, cfg, tokens, lens, table, kp2, vp2, append=False)
+    np.testing.assert_array_equal(l1, l2)
+    np.testing.assert_array_equal(n1, n2)
+    for a, b in zip(kp + vp, kp2 + vp2):
+        np.testing.assert_array_equal(a, b)
+
+
 def test_argmax_ties_lowest_index():
     x = np.array([[1.0, 3.0, 3.0, 2.0], [5.0, 5.0, 5.0, 5.0]])
     np.testing.assert_array_equal(ops.argmax(x), [1, 0])
