@@ -1,8 +1,8 @@
 """Parity of the tensor-core GEMV (exact integer fp16 weights on mma.sync, block scale in fp32)
 with the float64 oracle, through the C ABI.
 
-The path serves b2d_gemv for 32-block quantized weights (and fp16 weights when enabled), so the
-cases cover what changes inside it: fp16 activations used as they are vs hi + lo fp16 columns
+The path serves b2d_gemv for fp16 and 32-block quantized weights, so the cases cover what changes
+inside it: fp16 activations used as they are vs hi + lo fp16 columns
 (fp32 input or the fused RMSNorm), token groups (16 / 8 per pass over W), K slices per row tile
 (small K: one slice, several row tiles per CTA), ragged row counts, every epilogue, activations
 far from 1 in magnitude (the per-token power-of-two scale), and agreement with the CUDA-core path
