@@ -553,26 +553,24 @@ def run_ours(args) -> None:
     ms_e2e = max_over_ranks(e2.elapsed_time(e3)) / args.steps
 
     # ---- prefill of one 512-token prompt (b2d_decoder_prefill: chunks of BATCH positions per
-    # step), the reference's pp512 measurement; it rewrites sequence 0's first 512 positions, so
-    # it runs after everything above
-    PP = 512
-    pp_ids = torch.from_numpy(np.random.default_rng(SEED_TOK + 1).integers(0, shape.vocab, size=PP).astype(np.int32)).to(dev)
-    seq0 = table[0].contiguous()
-    pp_next = torch.empty(1, dtype=torch.int32, device=dev)
-    torch.cuda.synchronize()
-    for _ in range(2):
-        eng.prefill(pp_ids, seq0, 0, next_token=pp_next)
-    torch.cuda.synchronize()
-    barrier()
-    pp_reps = 5
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record(s)
-    for _ in range(pp_reps):
-        eng.prefill(pp_ids, seq0, 0, next_token=pp_next)
-    p1.record(s)
-    p1.synchronize()
-    barrier()
-    ms_pp = max_over_ranks(p0.elapsed_time(p1)) / pp_reps
+    # step), the reference's pp512 measurement, on one GPU (tensor-parallel prefill has no GPU
+    # parity test yet); it rewrites sequence 0's first 512 positions, so it runs after the above
+    PP, pp_reps, ms_pp = 512, 5, None
+    if world == 1:
+        pp_ids = torch.from_numpy(np.random.default_rng(SEED_TOK + 1).integers(0, shape.vocab, size=PP).astype(np.int32)).to(dev)
+        seq0 = table[0].contiguous()
+        pp_next = torch.empty(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        for _ in range(2):
+            eng.prefill(pp_ids, seq0, 0, next_token=pp_next)
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(s)
+        for _ in range(pp_reps):
+            eng.prefill(pp_ids, seq0, 0, next_token=pp_next)
+        p1.record(s)
+        p1.synchronize()
+        ms_pp = p0.elapsed_time(p1) / pp_reps
 
     peak, peak_kind = peaks()
     out = {
@@ -606,14 +604,15 @@ def run_ours(args) -> None:
         },
         "gpu_launches": int(launches_per_step * args.steps),
         "clocks": clk.summary(),
-        "prefill": {
+    }
+    if ms_pp is not None:
+        out["prefill"] = {
             "tokens": PP,
             "ms": ms_pp,
             "tokens_per_s": PP / (ms_pp / 1e3),
             "chunk": BATCH,
             "note": f"one {PP}-token prompt per call through b2d_decoder_prefill ({BATCH} positions per tcgen05 step, K/V written before attention); device-timed, mean of {pp_reps} calls",
-        },
-    }
+        }
 
     if rank == 0 and world == 1 and not args.no_ops:
         res = op_benchmarks(peak)
