@@ -109,3 +109,84 @@ def test_tp_decode_step_matches_oracle(batch, collective, world):
     for r in range(1, world):
         np.testing.assert_array_equal(got[0][1], got[r][1])  # every rank agrees on the tokens
     np.testing.assert_array_equal(got[0][1], np.argmax(logits, axis=1))
+
+
+def _prefill_rank(rank, world, port, q):
+    """One rank of a tensor-parallel prefill: 40 prompt tokens (a 32-row tensor-core chunk and an
+    8-row CUDA-core chunk), then the last position's logits shard."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, share_nccl_id
+    from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    try:
+        cfg, w, ids, table_row = _prefill_case()
+        shape = ModelShape(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
+        eng = DecodeEngine(shape, max_batch=32, max_ctx=128, n_blocks=8, tp_rank=rank, tp_size=world, nccl_id=share_nccl_id(rank), device=dev)
+        eng.alloc_kv()
+        eng.load_weights({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()})
+        ids_d = torch.tensor(np.asarray(ids, np.int32), device=dev)
+        tb = torch.from_numpy(table_row).to(dev)
+        logits = torch.empty(eng.lm_rows, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        nxt = eng.prefill(ids_d, tb, 0, logits=logits)
+        eng.stream.synchronize()
+        eng.check()
+        q.put((rank, logits.cpu().numpy(), int(nxt.item())))
+        eng.close()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+def _prefill_case():
+    from oracle import step as S
+
+    # 16 / 8 heads: at TP8 each rank holds 2 query heads and 1 KV head (256 QKV rows)
+    cfg = S.ModelConfig(512, 2, 16, 8, 64, 2048, 2048, 1e-5, 500000.0)
+    w = S.synth_weights(cfg, seed=41)
+    ids = np.random.default_rng(42).integers(0, cfg.vocab, size=40).tolist()
+    return cfg, w, ids, np.arange(8, dtype=np.int32)
+
+
+@pytest.mark.parametrize(
+    "world",
+    [pytest.param(w, marks=pytest.mark.skipif(torch.cuda.device_count() < w, reason=f"needs {w} GPUs")) for w in (2, 8)],
+)
+@pytest.mark.timeout(600)
+def test_tp_prefill_matches_oracle(world):
+    """b2d_decoder_prefill is collective: every rank prefills its heads' K/V and shard of the
+    model; the concatenated last-position logits match the oracle run token by token."""
+    from oracle import step as S
+    from tests._tol import assert_norm_close
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_prefill_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        rank, lg, nx = q.get(timeout=500)
+        got[rank] = (lg, nx)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    cfg, w, ids, table_row = _prefill_case()
+    shape = (8, cfg.n_kv_heads, 16, cfg.head_dim)
+    kp = [np.zeros(shape, np.float16) for _ in range(cfg.n_layers)]
+    vp = [np.zeros(shape, np.float16) for _ in range(cfg.n_layers)]
+    ref = None
+    for i, t in enumerate(ids):
+        ref, _ = S.decode_step(w, cfg, [t], [i], table_row[None, :], kp, vp)
+    logits = np.concatenate([got[r][0] for r in range(world)])
+    assert_norm_close(logits, ref[0], 2e-3, what=f"tp{world} prefill logits")
+    for r in range(1, world):
+        assert got[r][1] == got[0][1]  # every rank agrees on the next token
+    assert got[0][1] == int(np.argmax(logits))
