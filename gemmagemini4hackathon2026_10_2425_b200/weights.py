@@ -13,6 +13,13 @@ Tensor names: embed, l{i}.attn_norm, l{i}.wqkv (rows [q | k | v]), l{i}.wo, l{i}
 l{i}.wgate, l{i}.wup, l{i}.wdown, final_norm, and lm_head when the embeddings are not tied; fp16
 matrices, fp32 norms.  Files of this format load directly into DecodeEngine
 (`DecodeEngine.load_weights_file`), sharded per tensor-parallel rank on the way.
+
+Extension (no reference counterpart; the 32-block formats of include/b200dec.h): a projection
+matrix may be stored quantized as its integer tensor under its own name -- int8 [M, K] ("q8_32")
+or uint8 [M, K/2] with element 2j in the low nibble and value (n ^ 8) - 8 ("q4_32") -- plus
+`<name>.scales` fp16 [M, K/32], and a "quant" key in the matrix's header entry.  The arrays are
+exactly the operands b2d_gemv / b2d_gemm_tc_q take; readers that do not know the key (the
+reference's JSON decoding ignores unknown keys) see plain integer tensors.
 """
 
 from __future__ import annotations
@@ -28,6 +35,8 @@ from .tp import ModelShape
 
 ALIGN = 256
 PAGE = 16384
+QUANT_FORMATS = ("q8_32", "q4_32")
+QUANT_MATRICES = ("wqkv", "wo", "wgate", "wup", "wdown")  # per-layer projections
 HEADER_RESERVE = 64 * 1024  # the reference converter's fixed header prefix
 
 
@@ -36,6 +45,7 @@ class WeightsFile:
     config: dict
     tensors: dict[str, np.ndarray]  # read-only views of the mapped file
     path: Path
+    quant: dict[str, str] | None = None  # matrix name -> "q8_32" / "q4_32"
 
 
 def read_weights(path: str | Path) -> WeightsFile:
@@ -48,8 +58,12 @@ def read_weights(path: str | Path) -> WeightsFile:
     if 8 + hlen > raw.size:
         raise ValueError(f"{path}: header length {hlen} exceeds the file")
     header = json.loads(raw[8 : 8 + hlen].tobytes().decode("utf-8"))
-    tensors = {}
+    tensors, quant = {}, {}
     for name, meta in header["tensors"].items():
+        if "quant" in meta:
+            if meta["quant"] not in QUANT_FORMATS:
+                raise ValueError(f"{path}: tensor {name} has unknown quantization {meta['quant']!r}")
+            quant[name] = meta["quant"]
         dt = np.dtype(meta["dtype"])
         shape = tuple(int(d) for d in meta["shape"])
         off = int(meta["offset"])
@@ -57,16 +71,25 @@ def read_weights(path: str | Path) -> WeightsFile:
         if off % ALIGN or off + n > raw.size:
             raise ValueError(f"{path}: tensor {name} at {off} (+{n} B) is misaligned or out of range")
         tensors[name] = raw[off : off + n].view(dt).reshape(shape)
-    return WeightsFile(header["config"], tensors, path)
+    for name in quant:
+        if name + ".scales" not in tensors:
+            raise ValueError(f"{path}: quantized tensor {name} has no {name}.scales")
+    return WeightsFile(header["config"], tensors, path, quant)
 
 
-def write_weights(path: str | Path, config: dict, tensors: dict[str, np.ndarray]) -> int:
-    """Write tensors (in the given order) in the reference's layout; returns the file size."""
+def write_weights(
+    path: str | Path, config: dict, tensors: dict[str, np.ndarray], quant: dict[str, str] | None = None
+) -> int:
+    """Write tensors (in the given order) in the reference's layout; returns the file size.
+    `quant` marks quantized matrices (their `<name>.scales` must be among the tensors)."""
+    quant = quant or {}
     off = HEADER_RESERVE
     meta = {}
     for name, arr in tensors.items():
         off = -(-off // ALIGN) * ALIGN
         meta[name] = {"offset": off, "shape": list(arr.shape), "dtype": str(arr.dtype)}
+        if name in quant:
+            meta[name]["quant"] = quant[name]
         off += arr.nbytes
     total = -(-off // PAGE) * PAGE
     header = json.dumps({"config": config, "tensors": meta}).encode()
@@ -140,8 +163,70 @@ def inv_freq_from_config(cfg: dict) -> np.ndarray:
 
 def tensors_for_engine(wf: WeightsFile) -> dict[str, np.ndarray]:
     """The file's tensors under the names DecodeEngine.load_weights takes (lm_head falls back to
-    the tied embedding)."""
+    the tied embedding).  Quantized matrices become fp16(scale * q) -- the operand the tcgen05
+    quantized GEMM feeds its MMA -- since the decode step's projections are fp16."""
     t = dict(wf.tensors)
+    for name, fmt in (wf.quant or {}).items():
+        t[name] = dequantize(t[name], t.pop(name + ".scales"), fmt).astype(np.float16)
     if "lm_head" not in t:
         t["lm_head"] = t["embed"]
     return t
+
+
+# ---- 32-block quantization (the formats of include/b200dec.h) -------------------------------
+
+
+def quantize(w: np.ndarray, fmt: str) -> tuple[np.ndarray, np.ndarray]:
+    """Symmetric absmax quantization of a [M, K] matrix (K % 32 == 0) into 32-element blocks:
+    scale = fp16(max|w| / qmax) (qmax 127 for q8, 7 for q4), q = clip(rint(w / scale)).
+    Returns (q, scales): int8 [M, K] or packed uint8 [M, K/2]; fp16 [M, K/32]."""
+    if fmt not in QUANT_FORMATS:
+        raise ValueError(f"unknown format {fmt!r}")
+    w = np.asarray(w, dtype=np.float32)
+    m, k = w.shape
+    if k % 32:
+        raise ValueError("K must be a multiple of 32")
+    qmax, qmin = (127, -127) if fmt == "q8_32" else (7, -8)
+    blocks = w.reshape(m, k // 32, 32)
+    scales = (np.abs(blocks).max(axis=2) / qmax).astype(np.float16)
+    s32 = scales.astype(np.float32)[..., None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(s32 > 0, np.rint(blocks / s32), 0.0)
+    q = np.clip(q, qmin, qmax).astype(np.int8).reshape(m, k)
+    return (q if fmt == "q8_32" else pack_q4(q)), scales
+
+
+def pack_q4(q: np.ndarray) -> np.ndarray:
+    """int8 values in [-8, 7], [M, K] -> uint8 [M, K/2]: element 2j in the low nibble."""
+    n = (np.asarray(q, dtype=np.int16) & 0xF).astype(np.uint8)
+    return (n[:, 0::2] | (n[:, 1::2] << 4)).astype(np.uint8)
+
+
+def dequantize(q: np.ndarray, scales: np.ndarray, fmt: str) -> np.ndarray:
+    """fp32 [M, K] = float(scale) * q, exact."""
+    if fmt == "q8_32":
+        v = np.asarray(q, dtype=np.int8).astype(np.float32)
+    else:
+        p = np.asarray(q, dtype=np.uint8)
+        lo = ((p & 0xF) ^ 8).astype(np.float32) - 8.0
+        hi = (((p >> 4) & 0xF) ^ 8).astype(np.float32) - 8.0
+        v = np.empty((p.shape[0], p.shape[1] * 2), np.float32)
+        v[:, 0::2], v[:, 1::2] = lo, hi
+    m, k = v.shape
+    return (v.reshape(m, k // 32, 32) * np.asarray(scales, np.float32)[..., None]).reshape(m, k)
+
+
+def quantize_file(src: str | Path, dst: str | Path, fmt: str) -> int:
+    """Rewrite a weights file with every per-layer projection (wqkv, wo, wgate, wup, wdown)
+    quantized to `fmt`; embeddings, LM head and norms stay as they are.  Returns the size."""
+    wf = read_weights(src)
+    out, quant = {}, {}
+    for name, t in wf.tensors.items():
+        if name.split(".")[-1] in QUANT_MATRICES and t.ndim == 2 and name not in (wf.quant or {}):
+            q, sc = quantize(np.asarray(t), fmt)
+            out[name], out[name + ".scales"] = q, sc
+            quant[name] = fmt
+        else:
+            out[name] = np.asarray(t)
+    quant.update(wf.quant or {})
+    return write_weights(dst, wf.config, out, quant)

@@ -56,3 +56,69 @@ def test_rejects_truncated_file(tmp_path):
     bad.write_bytes(FILE.read_bytes()[: 70000])
     with pytest.raises(ValueError):
         W.read_weights(bad)
+
+
+# ---- quantized projections (32-block q8 / q4, the formats of include/b200dec.h) --------------
+
+
+@pytest.mark.parametrize("fmt", ["q8_32", "q4_32"])
+def test_quantize_matches_the_format(fmt):
+    """quantize() produces the header's layout: the oracle's independent dequantizer reads it back
+    bit-exactly, every element is within half a step of the input, zero blocks stay zero."""
+    from oracle import ops as O
+
+    r = np.random.default_rng(3)
+    w = (r.standard_normal((48, 256)) * 0.02).astype(np.float16)
+    w[5, 64:96] = 0  # an all-zero block
+    q, sc = W.quantize(w, fmt)
+    assert sc.dtype == np.float16 and sc.shape == (48, 8)
+    d = W.dequantize(q, sc, fmt)
+    ref = O.dequant_q8_32(q, sc) if fmt == "q8_32" else O.dequant_q4_32(q, sc)
+    np.testing.assert_array_equal(d.view(np.uint32), ref.view(np.uint32))
+    step = np.repeat(sc.astype(np.float32), 32, axis=1)
+    assert np.all(np.abs(d - w.astype(np.float32)) <= 0.5 * step * (1 + 2e-3) + 1e-12)
+    assert not d[5, 64:96].any()
+    if fmt == "q8_32":
+        assert q.dtype == np.int8 and q.shape == (48, 256) and np.abs(q).max() <= 127
+    else:
+        assert q.dtype == np.uint8 and q.shape == (48, 128)
+        np.testing.assert_array_equal(q, O.pack_q4(O.unpack_q4(q)))  # element 2j in the low nibble
+
+
+@pytest.mark.parametrize("fmt", ["q8_32", "q4_32"])
+def test_quantized_file_round_trip(tmp_path, fmt):
+    out = tmp_path / f"{fmt}.bin"
+    size = W.quantize_file(FILE, out, fmt)
+    assert size % W.PAGE == 0 and size < FILE.stat().st_size
+    src, wf = W.read_weights(FILE), W.read_weights(out)
+    assert wf.config == src.config
+    mats = {f"l{i}.{n}" for i in range(2) for n in W.QUANT_MATRICES}
+    assert set(wf.quant) == mats and set(wf.quant.values()) == {fmt}
+    for name in mats:
+        q, sc = W.quantize(np.asarray(src.tensors[name]), fmt)
+        np.testing.assert_array_equal(wf.tensors[name], q)
+        np.testing.assert_array_equal(wf.tensors[name + ".scales"], sc)
+    for name in ("embed", "final_norm", "l0.attn_norm"):  # untouched
+        np.testing.assert_array_equal(wf.tensors[name], src.tensors[name])
+    # the engine's view: fp16(scale * q) under the plain names, no .scales entries
+    t = W.tensors_for_engine(wf)
+    assert not any(k.endswith(".scales") for k in t)
+    assert t["l0.wqkv"].dtype == np.float16 and t["l0.wqkv"].shape == src.tensors["l0.wqkv"].shape
+    np.testing.assert_array_equal(
+        t["l1.wdown"], W.dequantize(wf.tensors["l1.wdown"], wf.tensors["l1.wdown.scales"], fmt).astype(np.float16)
+    )
+    # a copy keeps the quantization marks
+    W.write_weights(tmp_path / "copy.bin", wf.config, {k: np.asarray(v) for k, v in wf.tensors.items()}, wf.quant)
+    assert W.read_weights(tmp_path / "copy.bin").quant == wf.quant
+
+
+def test_quantized_file_errors(tmp_path):
+    wf = W.read_weights(FILE)
+    t = {k: np.asarray(v) for k, v in wf.tensors.items()}
+    with pytest.raises(ValueError):
+        W.quantize(np.zeros((4, 48), np.float16), "q8_32")  # K not a multiple of 32
+    with pytest.raises(ValueError):
+        W.quantize(np.zeros((4, 64), np.float16), "q5_32")
+    W.write_weights(tmp_path / "bad.bin", wf.config, t, {"l0.wo": "q8_32"})  # no l0.wo.scales
+    with pytest.raises(ValueError):
+        W.read_weights(tmp_path / "bad.bin")
