@@ -15,8 +15,8 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "b200dec.h"
 
 OK, ERR_NULL, ERR_SHAPE, ERR_ALIGN, ERR_UNSUPPORTED, ERR_WORKSPACE = 0, 1, 2, 3, 4, 5
 ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_STATE = 6, 7, 8, 9
-F32, F16, Q8_32, Q4_32 = 0, 1, 2, 3
-EPI_STORE, EPI_ADD, EPI_GELU_MUL, EPI_SWIGLU, EPI_ARGMAX = 0, 1, 2, 3, 4
+F32, F16, Q8_32, Q4_32, F16X2 = 0, 1, 2, 3, 4
+EPI_STORE, EPI_ADD, EPI_GELU_MUL, EPI_SWIGLU, EPI_ARGMAX, EPI_SILU_MUL = 0, 1, 2, 3, 4, 5
 
 P = C.c_void_p
 I = C.c_int
@@ -67,6 +67,9 @@ SIGNATURES = {
     "b2d_gemm_tc_workspace_bytes": (Z, [I, I, I, I]),
     "b2d_gemm_tc": (I, [P, P, P, I, I, I, P, I, P, I, I, I, P, P, P, I, P, Z, P]),
     "b2d_gemm_tc_q": (I, [I, P, P, P, I, I, I, P, I, P, I, I, I, P, Z, P]),
+    "b2d_gemm_tc_ex": (I, [I, P, P, P, I, I, I, P, I, P, I, I, I, P, P, P, I, P, Z, P]),
+    "b2d_gemm_tc_q_ex": (I, [I, I, P, P, P, I, I, I, P, I, P, I, I, I, P, Z, P]),
+    "b2d_add_rmsnorm": (I, [P, P, P, Fl, I, P, I, I, P]),
     "b2d_tc_packed_bytes": (Z, [I, I]),
     "b2d_tc_pack_f16": (I, [P, I, I, I, P, P]),
     "b2d_gemm_tc_packed": (I, [P, P, P, I, I, I, P, I, P, I, I, I, P, P, P, I, P, Z, P]),
@@ -83,6 +86,7 @@ SIGNATURES = {
         [P, I, I, P, P, P, I, I, P, P, I, I, I, I, I, Fl, I, I, P, I, I, P, Z, P],
     ),
     "b2d_paged_decode_attn_noalloc_max_scratch_bytes": (Z, []),
+    "b2d_paged_decode_attn_noalloc_error": (I, []),
     "b2d_paged_decode_attn_noalloc": (
         I,
         [P, I, I, P, P, P, I, I, P, P, I, I, I, I, I, Fl, I, I, P, I, I, P],
@@ -92,6 +96,7 @@ SIGNATURES = {
     "b2d_decoder_create": (I, [C.POINTER(ModelConfig), I, I, P, C.POINTER(P)]),
     "b2d_decoder_destroy": (I, [P]),
     "b2d_decoder_set_layer": (I, [P, I, P, P, P, P, P, P, P, P, P]),
+    "b2d_decoder_set_layer_q": (I, [P, I, I, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "b2d_decoder_set_head": (I, [P, P, P, I, P]),
     "b2d_decoder_step": (I, [P, P, P, P, I, P, P, I, P]),
     "b2d_decoder_peer_collectives": (I, [P]),

@@ -45,6 +45,7 @@ struct AttnParams {
   int append;
   void* out;
   int out_f16;
+  uint16_t* out_lo;  // B2D_F16X2 output: the lo plane (nullptr otherwise)
   int ldout;
   int max_ctx;     // every ctx_lens[b] + 1 must be <= max_ctx
   int chunk;       // keys per CTA (multiple of 16)
@@ -85,7 +86,7 @@ __device__ void chunk_finish(const AttnParams& p, const float* st, int b, int kv
       const float r = o / lsum;
       const size_t oi = (size_t)b * p.ldout + (size_t)(kvh * G + g) * HD + d;
       if (p.out_f16)
-        reinterpret_cast<uint16_t*>(p.out)[oi] = f2h(r);
+        store_f16_split(reinterpret_cast<uint16_t*>(p.out), p.out_lo, oi, r);
       else
         reinterpret_cast<float*>(p.out)[oi] = r;
     } else {
@@ -155,7 +156,7 @@ __device__ void chunk_finish(const AttnParams& p, const float* st, int b, int kv
     }
     const size_t oi = (size_t)b * p.ldout + (size_t)(kvh * G + g) * HD + d;
     if (p.out_f16)
-      reinterpret_cast<uint16_t*>(p.out)[oi] = f2h(r);
+      store_f16_split(reinterpret_cast<uint16_t*>(p.out), p.out_lo, oi, r);
     else
       reinterpret_cast<float*>(p.out)[oi] = r;
   }
@@ -958,7 +959,8 @@ int paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages, ui
     return B2D_ERR_SHAPE;
   if (head_dim != 64 && head_dim != 128 && head_dim != 256) return B2D_ERR_UNSUPPORTED;
   if (qkv_dtype != B2D_F32 && qkv_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
-  if (out_dtype != B2D_F32 && out_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
+  if (out_dtype != B2D_F32 && out_dtype != B2D_F16 && out_dtype != B2D_F16X2)
+    return B2D_ERR_UNSUPPORTED;
   if (ldqkv < (n_heads + 2 * n_kv_heads) * head_dim || ldout < n_heads * head_dim)
     return B2D_ERR_SHAPE;
   if (!aligned16(k_pages) || !aligned16(v_pages)) return B2D_ERR_ALIGN;
@@ -983,7 +985,8 @@ int paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages, ui
   prm.window = window;
   prm.append = append;
   prm.out = out;
-  prm.out_f16 = out_dtype == B2D_F16;
+  prm.out_f16 = out_dtype != B2D_F32;
+  prm.out_lo = out_dtype == B2D_F16X2 ? static_cast<uint16_t*>(out) + (size_t)batch * ldout : nullptr;
   prm.ldout = ldout;
   prm.max_ctx = max_ctx;
   prm.chunk = attn_chunk_tokens(batch, n_kv_heads, max_ctx);

@@ -42,22 +42,23 @@ int add_f32(float*, const float*, size_t, cudaStream_t);
 int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                    const float*, int, int, int, int, cudaStream_t);
 int attn_chunk_tokens(int, int, int);
-int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, int, int, cudaStream_t);
-int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*, int,
-                      int, cudaStream_t);
+int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
+                    cudaStream_t);
+int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*,
+                      uint16_t*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
-int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
-int tc_gemm_q(int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
-              const float*, int, int, int, void*, size_t, cudaStream_t);
+int tc_gemm_q(int, int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int);
 int tc_gemm_packed(const uint8_t*, const uint8_t*, const uint16_t*, int, int, int, void*, int,
                    const float*, int, int, int, float*, int*, float*, int, void*, size_t,
                    cudaStream_t);
 size_t tc_packed_bytes(int, int);
 int tc_pack_f16(const uint16_t*, int, int, int, void*, cudaStream_t);
 int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
-                             float*, const float*, float, uint16_t*, int, int, long long, int*,
-                             cudaStream_t);
+                             float*, const float*, float, uint16_t*, uint16_t*, int, int,
+                             long long, int*, cudaStream_t);
 int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, uint32_t*, int,
                      int, int, int, int*, long long, int*, cudaStream_t);
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
@@ -175,12 +176,21 @@ int b2d_add_f32(float* x, const float* p, size_t n, b2d_stream_t stream) {
 
 int b2d_add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps, uint16_t* out,
                         int rows, int D, b2d_stream_t stream) {
-  return add_rmsnorm_f16(x, p, gamma, eps, out, rows, D, S(stream));
+  return add_rmsnorm_f16(x, p, gamma, eps, out, nullptr, rows, D, S(stream));
+}
+
+int b2d_add_rmsnorm(float* x, const float* p, const float* gamma, float eps, int out_dtype,
+                    void* out, int rows, int D, b2d_stream_t stream) {
+  if (out_dtype != B2D_F16 && out_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
+  uint16_t* o = static_cast<uint16_t*>(out);
+  return add_rmsnorm_f16(x, p, gamma, eps, o,
+                         (out_dtype == B2D_F16X2 && o) ? o + (size_t)rows * D : nullptr, rows, D,
+                         S(stream));
 }
 
 int b2d_embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
                           float eps, uint16_t* out, int D, int batch, b2d_stream_t stream) {
-  return embed_rmsnorm_f16(E, tokens, x, gamma, eps, out, D, batch, S(stream));
+  return embed_rmsnorm_f16(E, tokens, x, gamma, eps, out, nullptr, D, batch, S(stream));
 }
 
 size_t b2d_gemm_tc_workspace_bytes(int M, int K, int batch, int epilogue) {
@@ -191,8 +201,17 @@ int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int 
                 int y_dtype, void* y, int ldy, const float* aux, int M, int K, int batch,
                 float* logits, int* tokens, float* max_vals, int index_offset, void* workspace,
                 size_t workspace_bytes, b2d_stream_t stream) {
-  return tc_gemm(W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits, tokens,
-                 max_vals, index_offset, workspace, workspace_bytes, S(stream));
+  return tc_gemm(B2D_F16, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits,
+                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream));
+}
+
+int b2d_gemm_tc_ex(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
+                   int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+                   int K, int batch, float* logits, int* tokens, float* max_vals,
+                   int index_offset, void* workspace, size_t workspace_bytes,
+                   b2d_stream_t stream) {
+  return tc_gemm(x_dtype, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits,
+                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream));
 }
 
 size_t b2d_tc_packed_bytes(int M, int K) { return tc_packed_bytes(M, K); }
@@ -214,16 +233,24 @@ int b2d_gemm_tc_packed(const void* Wp, const void* Wp_up, const uint16_t* X, int
 int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X, int ldx,
                   int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
                   int batch, void* workspace, size_t workspace_bytes, b2d_stream_t stream) {
-  return tc_gemm_q(w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
-                   workspace, workspace_bytes, S(stream));
+  return tc_gemm_q(B2D_F16, w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
+                   batch, workspace, workspace_bytes, S(stream), nullptr, 0);
+}
+
+int b2d_gemm_tc_q_ex(int x_dtype, int w_dtype, const void* q, const uint16_t* scales,
+                     const uint16_t* X, int ldx, int epilogue, int y_dtype, void* y, int ldy,
+                     const float* aux, int M, int K, int batch, void* workspace,
+                     size_t workspace_bytes, b2d_stream_t stream) {
+  return tc_gemm_q(x_dtype, w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
+                   batch, workspace, workspace_bytes, S(stream), nullptr, 0);
 }
 
 int b2d_tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs,
                                  uint32_t* epochs, int rank, int tp, int slot0, float* x,
                                  const float* gamma, float eps, uint16_t* out16, int D, int rows,
                                  long long timeout_ns, int* err, b2d_stream_t stream) {
-  return tp_allreduce_add_rmsnorm(parts, sigs, epochs, rank, tp, slot0, x, gamma, eps, out16, D,
-                                  rows, timeout_ns, err, S(stream));
+  return tp_allreduce_add_rmsnorm(parts, sigs, epochs, rank, tp, slot0, x, gamma, eps, out16,
+                                  nullptr, D, rows, timeout_ns, err, S(stream));
 }
 
 int b2d_tp_argmax_gather(const float* const* vals, const int* const* idxs, uint32_t* const* sigs,

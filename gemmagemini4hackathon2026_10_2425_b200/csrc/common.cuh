@@ -63,6 +63,24 @@ __device__ __forceinline__ float2 h2f2(uint32_t u) {
 __device__ __forceinline__ float h2f(uint16_t u) { return __half2float(__ushort_as_half(u)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
+// Four fp32 values as fp16 hi + lo planes (B2D_F16X2): hi = fp16(v), lo = fp16(v - hi).
+// Returns the hi plane's 8 bytes; the lo plane's go to *lo.
+__device__ __forceinline__ uint2 split4_f16(float a, float b, float c, float d, uint2* lo) {
+  const __half2 h01 = __floats2half2_rn(a, b), h23 = __floats2half2_rn(c, d);
+  const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+  const __half2 l01 = __floats2half2_rn(a - f01.x, b - f01.y);
+  const __half2 l23 = __floats2half2_rn(c - f23.x, d - f23.y);
+  *lo = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+}
+
+// Store v as fp16 at out[i] and, if out_lo, its remainder fp16(v - hi) at out_lo[i].
+__device__ __forceinline__ void store_f16_split(uint16_t* out, uint16_t* out_lo, size_t i, float v) {
+  const uint16_t hi = f2h(v);
+  out[i] = hi;
+  if (out_lo) out_lo[i] = f2h(v - h2f(hi));
+}
+
 // Signed bytes -> floats without I2F: place byte^0x80 under the exponent of 2^23 and subtract
 // (2^23 + 128).  Exact for every int8 value.
 __device__ __forceinline__ float byte_to_float(uint32_t biased_word, int i) {

@@ -40,22 +40,26 @@ int embed_f16(const uint16_t*, const int*, float*, int, int, cudaStream_t);
 int argmax_combine(const float*, const int*, int, int, int*, cudaStream_t);
 int add_f32(float*, const float*, size_t, cudaStream_t);
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
+size_t attn_ws_header_bytes(int batch, int n_kv_heads);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
                       void*, size_t, cudaStream_t);
 int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                    const float*, int, int, int, int, cudaStream_t);
-int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, int, int, cudaStream_t);
-int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*, int,
-                      int, cudaStream_t);
+int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
+                    cudaStream_t);
+int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*,
+                      uint16_t*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
-int tc_gemm(const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
-int tc_gemm_multi_store(const uint16_t*, const uint16_t*, int, float* const*, int, int, int, int,
-                        int, void*, size_t, cudaStream_t);
+int tc_gemm_multi_store(int, const uint16_t*, const uint16_t*, int, float* const*, int, int, int,
+                        int, int, void*, size_t, cudaStream_t);
+int tc_gemm_q(int, int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int);
 int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
-                             float*, const float*, float, uint16_t*, int, int, long long, int*,
-                             cudaStream_t);
+                             float*, const float*, float, uint16_t*, uint16_t*, int, int,
+                             long long, int*, cudaStream_t);
 int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, uint32_t*, int,
                      int, int, int, int*, long long, int*, cudaStream_t);
 }  // namespace b2d
@@ -70,7 +74,7 @@ using namespace b2d;
 
 struct Layer {
   const float* attn_norm = nullptr;
-  const uint16_t* wqkv = nullptr;
+  const uint16_t* wqkv = nullptr;  // fp16 weights, or the raw q8_32 / q4_32 integers
   const uint16_t* wo = nullptr;
   const float* ffn_norm = nullptr;
   const uint16_t* wgate = nullptr;
@@ -78,6 +82,13 @@ struct Layer {
   const uint16_t* wdown = nullptr;
   uint16_t* k_pages = nullptr;
   uint16_t* v_pages = nullptr;
+  int wdt = B2D_F16;  // B2D_F16, B2D_Q8_32 or B2D_Q4_32 (all five projections)
+  // fp16 block scales [rows, K/32] of the quantized projections (nullptr for fp16 weights)
+  const uint16_t* sqkv = nullptr;
+  const uint16_t* so = nullptr;
+  const uint16_t* sgate = nullptr;
+  const uint16_t* sup = nullptr;
+  const uint16_t* sdown = nullptr;
 };
 
 struct GraphKey {
@@ -114,10 +125,11 @@ struct b2d_decoder {
   size_t attn_ws_bytes = 0;
   void* am_ws = nullptr;
   size_t am_ws_bytes = 0;
-  // tensor-core path (batch >= kTcMinBatch): fp16 activation operands + GEMM workspace
-  uint16_t* xn16 = nullptr;   // [B, D]   rmsnorm(x) * gamma, fp16
-  uint16_t* att16 = nullptr;  // [B, hq*HD]
-  uint16_t* h16 = nullptr;    // [B, fl]
+  // tensor-core path (batch >= kTcMinBatch): activation operands as B2D_F16X2 hi + lo fp16
+  // planes (a step of batch B keeps the lo plane B rows after the hi plane) + GEMM workspace
+  uint16_t* xn16 = nullptr;   // [2][B, D]   rmsnorm(x) * gamma
+  uint16_t* att16 = nullptr;  // [2][B, hq*HD]  attention output
+  uint16_t* h16 = nullptr;    // [2][B, fl]  SwiGLU output
   void* tc_ws = nullptr;
   size_t tc_ws_bytes = 0;
   // tensor parallelism: buffers the peers read (one IPC-shared allocation per rank)
@@ -157,20 +169,38 @@ static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 // Row-parallel projection (tensor cores) of this rank into buffer `buf`: with peer memory the
 // epilogue stores the partial straight into every rank's receive slot for this rank (the data
 // crosses NVLink while the GEMM finishes), else into the local slot for NCCL.
-static int tp_partial(b2d_decoder* h, int buf, const uint16_t* W, const uint16_t* X, int K, int B,
-                      cudaStream_t s) {
+static int tp_partial(b2d_decoder* h, int buf, int wdt, const uint16_t* W, const uint16_t* scales,
+                      const uint16_t* X, int K, int B, cudaStream_t s) {
   const int D = h->cfg.dim;
-  if (h->peer) {
-    float* ys[kMaxTp];
-    for (int r = 0; r < h->tp; ++r) ys[r] = h->recv[buf][r][h->rank];
-    return tc_gemm_multi_store(W, X, K, ys, h->tp, D, D, K, B, h->tc_ws, h->tc_ws_bytes, s);
-  }
-  return tc_gemm(W, nullptr, X, K, B2D_EPI_STORE, B2D_F32, h->recv[buf][h->rank][h->rank], D,
-                 nullptr, D, K, B, nullptr, nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
+  float* ys[kMaxTp];
+  int n_ys = 0;
+  if (h->peer)
+    for (int r = 0; r < h->tp; ++r) ys[n_ys++] = h->recv[buf][r][h->rank];
+  float* mine = h->peer ? nullptr : h->recv[buf][h->rank][h->rank];
+  if (wdt != B2D_F16)
+    return tc_gemm_q(B2D_F16X2, wdt, W, scales, X, K, B2D_EPI_STORE, B2D_F32, mine, D, nullptr, D,
+                     K, B, h->tc_ws, h->tc_ws_bytes, s, ys, n_ys);
+  if (h->peer)
+    return tc_gemm_multi_store(B2D_F16X2, W, X, K, ys, n_ys, D, D, K, B, h->tc_ws,
+                               h->tc_ws_bytes, s);
+  return tc_gemm(B2D_F16X2, W, nullptr, X, K, B2D_EPI_STORE, B2D_F32, mine, D, nullptr, D, K, B,
+                 nullptr, nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
+}
+
+// One projection of the tensor-core step: y = epilogue(W x) with x as B2D_F16X2 planes, on the
+// fp16 or the quantized tcgen05 GEMM by the layer's weight type.
+static int tc_proj(b2d_decoder* h, int wdt, const uint16_t* W, const uint16_t* scales,
+                   const uint16_t* X, int K, int epi, int y_dtype, void* y, int ldy, int M,
+                   const float* aux, int B, cudaStream_t s) {
+  if (wdt != B2D_F16)
+    return tc_gemm_q(B2D_F16X2, wdt, W, scales, X, K, epi, y_dtype, y, ldy, aux, M, K, B, h->tc_ws,
+                     h->tc_ws_bytes, s, nullptr, 0);
+  return tc_gemm(B2D_F16X2, W, nullptr, X, K, epi, y_dtype, y, ldy, aux, M, K, B, nullptr,
+                 nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
 }
 
 // Sum the ranks' row-parallel partials (buffer `buf`) into the residual x; with gamma, also
-// write fp16(rmsnorm(x) * gamma) to out16.  `pushed`: every rank's producer already stored its
+// write rmsnorm(x) * gamma to out16 as B2D_F16X2 planes of B rows.  `pushed`: every rank's producer already stored its
 // partial into this rank's receive slots (the tensor-core path), so the sum reads local memory;
 // otherwise each rank's partial sits in its own slot and the sum reads it over NVLink.
 static int tp_reduce(b2d_decoder* h, int buf, const float* gamma, uint16_t* out16, int B,
@@ -180,11 +210,13 @@ static int tp_reduce(b2d_decoder* h, int buf, const float* gamma, uint16_t* out1
     float* parts[kMaxTp];
     for (int r = 0; r < h->tp; ++r) parts[r] = pushed ? h->recv[buf][h->rank][r] : h->recv[buf][r][r];
     return tp_allreduce_add_rmsnorm(parts, h->sigs, h->epochs, h->rank, h->tp, 0, h->x, gamma,
-                                    h->cfg.eps, out16, D, B, kPeerTimeoutNs, h->err, s);
+                                    h->cfg.eps, out16, out16 ? out16 + (size_t)B * D : nullptr, D,
+                                    B, kPeerTimeoutNs, h->err, s);
   }
   float* mine = h->recv[buf][h->rank][h->rank];
   B2D_TRY(nccl_status(ncclAllReduce(mine, mine, (size_t)B * D, ncclFloat, ncclSum, h->comm, s)));
-  return gamma ? add_rmsnorm_f16(h->x, mine, gamma, h->cfg.eps, out16, B, D, s)
+  return gamma ? add_rmsnorm_f16(h->x, mine, gamma, h->cfg.eps, out16, out16 + (size_t)B * D, B,
+                                 D, s)
                : add_f32(h->x, mine, (size_t)B * D, s);
 }
 
@@ -219,8 +251,9 @@ static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
                            h->attn_ws, h->attn_ws_bytes, s);
 }
 
-// Tensor-core step (batch >= kTcMinBatch): activations enter each projection as fp16
-// (RMSNorm fused into the producer of the operand), weights are read once per step.
+// Tensor-core step (batch >= kTcMinBatch): every projection's activation operand enters as
+// B2D_F16X2 hi + lo fp16 planes (fp32 precision, like the reference's fp32 activations), with
+// RMSNorm fused into the producer of the operand; weights are read once per step.
 // next_tokens == nullptr skips the LM head (a prefill chunk whose outputs nobody reads).
 static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_lens,
                            const int* block_table, int B, int* next_tokens, float* logits,
@@ -230,35 +263,45 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   const bool tpar = h->tp > 1;
   void* ws = h->tc_ws;
   const size_t wsb = h->tc_ws_bytes;
-  B2D_TRY(embed_rmsnorm_f16(h->embed, tokens, h->x, h->layers[0].attn_norm, c.eps, h->xn16, D, B,
-                            s));
+  constexpr int X2 = B2D_F16X2;
+  uint16_t* const xn_lo = h->xn16 + (size_t)B * D;  // lo planes of this batch's operands
+  B2D_TRY(embed_rmsnorm_f16(h->embed, tokens, h->x, h->layers[0].attn_norm, c.eps, h->xn16, xn_lo,
+                            D, B, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = h->layers[l];
     const float* next_norm = l + 1 < c.n_layers ? h->layers[l + 1].attn_norm : h->final_norm;
     // QKV (column-parallel)
-    B2D_TRY(tc_gemm(L.wqkv, nullptr, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
-                    nullptr, h->qkv_l, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-    // RoPE + KV append + split-K attention -> fp16 operand of the O projection
-    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, B2D_F16, s));
-    // O projection (row-parallel) + residual, then RMSNorm(ffn) -> fp16
+    B2D_TRY(tc_proj(h, L.wdt, L.wqkv, L.sqkv, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
+                    h->qkv_l, nullptr, B, s));
+    // RoPE + KV append + split-K attention -> hi/lo operand of the O projection
+    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s));
+    // O projection (row-parallel) + residual, then RMSNorm(ffn) -> hi/lo
     if (!tpar) {
-      B2D_TRY(tc_gemm(L.wo, nullptr, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
-                      HQD, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, B, D, s));
+      B2D_TRY(tc_proj(h, L.wdt, L.wo, L.so, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, D,
+                      nullptr, B, s));
+      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, xn_lo, B, D, s));
     } else {
-      B2D_TRY(tp_partial(h, 0, L.wo, h->att16, HQD, B, s));
+      B2D_TRY(tp_partial(h, 0, L.wdt, L.wo, L.so, h->att16, HQD, B, s));
       B2D_TRY(tp_reduce(h, 0, L.ffn_norm, h->xn16, B, h->peer, s));
     }
-    // gate/up SwiGLU (column-parallel) -> fp16
-    B2D_TRY(tc_gemm(L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, B2D_F16, h->h16, h->fl, nullptr,
-                    h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-    // down (row-parallel) + residual, then the next RMSNorm -> fp16
-    if (!tpar) {
-      B2D_TRY(tc_gemm(L.wdown, nullptr, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
-                      h->fl, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
-      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, B, D, s));
+    // gate/up SwiGLU (column-parallel) -> hi/lo.  fp16 weights: one dual-matrix GEMM; quantized
+    // weights: the up projection into hid (fp32), then the gate projection times it.
+    if (L.wdt == B2D_F16) {
+      B2D_TRY(tc_gemm(X2, L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, X2, h->h16, h->fl, nullptr,
+                      h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
     } else {
-      B2D_TRY(tp_partial(h, 1, L.wdown, h->h16, h->fl, B, s));
+      B2D_TRY(tc_proj(h, L.wdt, L.wup, L.sup, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->hid, h->fl,
+                      h->fl, nullptr, B, s));
+      B2D_TRY(tc_proj(h, L.wdt, L.wgate, L.sgate, h->xn16, D, B2D_EPI_SILU_MUL, X2, h->h16, h->fl,
+                      h->fl, h->hid, B, s));
+    }
+    // down (row-parallel) + residual, then the next RMSNorm -> hi/lo
+    if (!tpar) {
+      B2D_TRY(tc_proj(h, L.wdt, L.wdown, L.sdown, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, D,
+                      nullptr, B, s));
+      B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, xn_lo, B, D, s));
+    } else {
+      B2D_TRY(tp_partial(h, 1, L.wdt, L.wdown, L.sdown, h->h16, h->fl, B, s));
       B2D_TRY(tp_reduce(h, 1, next_norm, h->xn16, B, h->peer, s));
     }
   }
@@ -266,12 +309,12 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   if (!next_tokens) return B2D_OK;
   const int offset = h->rank * h->lm_stride;
   if (!tpar) {
-    B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
-                    h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s));
+    B2D_TRY(tc_gemm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
+                    nullptr, h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s));
   } else {
-    B2D_TRY(tc_gemm(h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0, nullptr,
-                    h->lm_rows, D, B, logits, h->am_idx[h->rank], h->am_val[h->rank], offset, ws,
-                    wsb, s));
+    B2D_TRY(tc_gemm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
+                    nullptr, h->lm_rows, D, B, logits, h->am_idx[h->rank], h->am_val[h->rank],
+                    offset, ws, wsb, s));
     B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
   return B2D_OK;
@@ -315,34 +358,32 @@ static int enqueue_step(b2d_decoder* h, const int* tokens, const int* ctx_lens,
   B2D_TRY(embed_f16(h->embed, tokens, h->x, D, B, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = h->layers[l];
+    const int wd = L.wdt;
     // RMSNorm + QKV (column-parallel: this rank's heads)
-    B2D_TRY(gemv_dispatch(B2D_F16, L.wqkv, nullptr, nullptr, nullptr, B2D_F32, h->x, D,
-                          L.attn_norm, c.eps, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l, nullptr,
-                          h->qkv_l, D, B, s));
+    B2D_TRY(gemv_dispatch(wd, L.wqkv, L.sqkv, nullptr, nullptr, B2D_F32, h->x, D, L.attn_norm,
+                          c.eps, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l, nullptr, h->qkv_l, D, B,
+                          s));
     // RoPE + KV append + split-K GQA attention over the paged cache
     B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att, B2D_F32, s));
     // O projection (row-parallel) + residual
     if (!tpar) {
-      B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
-                            h->hq * HD, nullptr, 0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D,
-                            h->hq * HD, B, s));
+      B2D_TRY(gemv_dispatch(wd, L.wo, L.so, nullptr, nullptr, B2D_F32, h->att, h->hq * HD, nullptr,
+                            0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D, h->hq * HD, B, s));
     } else {
-      B2D_TRY(gemv_dispatch(B2D_F16, L.wo, nullptr, nullptr, nullptr, B2D_F32, h->att,
-                            h->hq * HD, nullptr, 0.f, B2D_EPI_STORE, B2D_F32,
-                            h->recv[0][h->rank][h->rank], D, nullptr, D, h->hq * HD, B, s));
+      B2D_TRY(gemv_dispatch(wd, L.wo, L.so, nullptr, nullptr, B2D_F32, h->att, h->hq * HD, nullptr,
+                            0.f, B2D_EPI_STORE, B2D_F32, h->recv[0][h->rank][h->rank], D, nullptr,
+                            D, h->hq * HD, B, s));
       B2D_TRY(tp_reduce(h, 0, nullptr, nullptr, B, false, s));
     }
     // RMSNorm + gate/up SwiGLU (column-parallel: this rank's FFN rows)
-    B2D_TRY(gemv_dispatch(B2D_F16, L.wgate, nullptr, L.wup, nullptr, B2D_F32, h->x, D,
-                          L.ffn_norm, c.eps, B2D_EPI_SWIGLU, B2D_F32, h->hid, h->fl, nullptr,
-                          h->fl, D, B, s));
+    B2D_TRY(gemv_dispatch(wd, L.wgate, L.sgate, L.wup, L.sup, B2D_F32, h->x, D, L.ffn_norm, c.eps,
+                          B2D_EPI_SWIGLU, B2D_F32, h->hid, h->fl, nullptr, h->fl, D, B, s));
     // down projection (row-parallel) + residual
     if (!tpar) {
-      B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
-                            nullptr, 0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D, h->fl, B,
-                            s));
+      B2D_TRY(gemv_dispatch(wd, L.wdown, L.sdown, nullptr, nullptr, B2D_F32, h->hid, h->fl, nullptr,
+                            0.f, B2D_EPI_ADD, B2D_F32, h->x, D, nullptr, D, h->fl, B, s));
     } else {
-      B2D_TRY(gemv_dispatch(B2D_F16, L.wdown, nullptr, nullptr, nullptr, B2D_F32, h->hid, h->fl,
+      B2D_TRY(gemv_dispatch(wd, L.wdown, L.sdown, nullptr, nullptr, B2D_F32, h->hid, h->fl,
                             nullptr, 0.f, B2D_EPI_STORE, B2D_F32, h->recv[1][h->rank][h->rank], D,
                             nullptr, D, h->fl, B, s));
       B2D_TRY(tp_reduce(h, 1, nullptr, nullptr, B, false, s));
@@ -503,7 +544,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
       (size_t)tp_size * B * 4,    (size_t)tp_size * B * 4,  (size_t)4,  (size_t)B * 4,
       (size_t)2 * B * 4,          (size_t)2 * B * c.max_blocks * 4,
       h->attn_ws_bytes,           h->am_ws_bytes,
-      (size_t)B * D * 2,          (size_t)B * h->hq * c.head_dim * 2, (size_t)B * h->fl * 2,
+      (size_t)2 * B * D * 2,      (size_t)2 * B * h->hq * c.head_dim * 2, (size_t)2 * B * h->fl * 2,
       h->tc_ws_bytes};
   size_t total = 0;
   for (size_t s : sizes) total += align256(s);
@@ -578,10 +619,26 @@ int b2d_decoder_peer_collectives(const b2d_decoder* h) { return h && h->peer ? 1
 
 int b2d_decoder_error(b2d_decoder* h) {
   if (!h) return B2D_ERR_NULL;
-  int v = 0;
-  B2D_TRY(cuda_status(cudaMemcpy(&v, h->err, sizeof(int), cudaMemcpyDeviceToHost)));
-  if (v) B2D_TRY(cuda_status(cudaMemset(h->err, 0, sizeof(int))));
-  return v;
+  // the steps may have run on any stream of this device (engine streams do not wait for the
+  // legacy default stream): wait for all of them before reading the error words
+  B2D_TRY(cuda_status(cudaDeviceSynchronize()));
+  // error words: the peer barriers' (h->err), the attention's and the tensor-core GEMMs'
+  // (first int of their workspaces; each of their bounded waits sets it when it gives up)
+  int words[3] = {0, 0, 0};
+  B2D_TRY(cuda_status(cudaMemcpy(&words[0], h->err, sizeof(int), cudaMemcpyDeviceToHost)));
+  B2D_TRY(cuda_status(cudaMemcpy(&words[1], h->attn_ws, sizeof(int), cudaMemcpyDeviceToHost)));
+  if (h->tc_ws_bytes)  // only decoders whose batch reaches the tensor-core path have one
+    B2D_TRY(cuda_status(cudaMemcpy(&words[2], h->tc_ws, sizeof(int), cudaMemcpyDeviceToHost)));
+  if (!(words[0] | words[1] | words[2])) return B2D_OK;
+  // A CTA whose wait gave up returned before its arrival on the split-K / argmax counters, so
+  // besides the error words the counters are reset too: later steps start from zero again.
+  B2D_TRY(cuda_status(cudaMemset(h->err, 0, sizeof(int))));
+  B2D_TRY(cuda_status(
+      cudaMemset(h->attn_ws, 0, attn_ws_header_bytes(h->cfg.max_batch, h->hk))));
+  if (h->tc_ws_bytes)
+    B2D_TRY(cuda_status(cudaMemset(h->tc_ws, 0, std::min<size_t>(h->tc_ws_bytes, 512))));
+  B2D_TRY(cuda_status(cudaDeviceSynchronize()));
+  return words[0] ? words[0] : B2D_ERR_TIMEOUT;
 }
 
 int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,
@@ -604,6 +661,40 @@ int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_norm,
     h->gen_exec = nullptr;
     h->gen_key = GraphKey();
   }
+  return B2D_OK;
+}
+
+int b2d_decoder_set_layer_q(b2d_decoder* h, int layer, int w_dtype, const float* attn_norm,
+                            const void* wqkv, const uint16_t* wqkv_scales, const void* wo,
+                            const uint16_t* wo_scales, const float* ffn_norm, const void* wgate,
+                            const uint16_t* wgate_scales, const void* wup,
+                            const uint16_t* wup_scales, const void* wdown,
+                            const uint16_t* wdown_scales, uint16_t* k_pages, uint16_t* v_pages) {
+  if (!h) return B2D_ERR_NULL;
+  if (w_dtype == B2D_F16)
+    return b2d_decoder_set_layer(h, layer, attn_norm, static_cast<const uint16_t*>(wqkv),
+                                 static_cast<const uint16_t*>(wo), ffn_norm,
+                                 static_cast<const uint16_t*>(wgate),
+                                 static_cast<const uint16_t*>(wup),
+                                 static_cast<const uint16_t*>(wdown), k_pages, v_pages);
+  if (w_dtype != B2D_Q8_32 && w_dtype != B2D_Q4_32) return B2D_ERR_UNSUPPORTED;
+  if (!wqkv_scales || !wo_scales || !wgate_scales || !wup_scales || !wdown_scales)
+    return B2D_ERR_NULL;
+  // every projection's K must hold whole 32-element blocks (the row-parallel shards included)
+  const b2d_model_config& c = h->cfg;
+  if (c.dim % 32 || (h->hq * c.head_dim) % 32 || h->fl % 32) return B2D_ERR_SHAPE;
+  B2D_TRY(b2d_decoder_set_layer(h, layer, attn_norm, static_cast<const uint16_t*>(wqkv),
+                                static_cast<const uint16_t*>(wo), ffn_norm,
+                                static_cast<const uint16_t*>(wgate),
+                                static_cast<const uint16_t*>(wup),
+                                static_cast<const uint16_t*>(wdown), k_pages, v_pages));
+  Layer& L = h->layers[layer];
+  L.wdt = w_dtype;
+  L.sqkv = wqkv_scales;
+  L.so = wo_scales;
+  L.sgate = wgate_scales;
+  L.sup = wup_scales;
+  L.sdown = wdown_scales;
   return B2D_OK;
 }
 

@@ -11,11 +11,15 @@
 // The array's name, used in host code, is only a host-side stand-in for the symbol, not a
 // device address.  So on the first call on each device, with that device current, this file
 // looks up the device address once with cudaGetSymbolAddress and caches it; kernels then get
-// that address.  That first call also zero-fills the array with a synchronous cudaMemset, so
-// it must come before any stream capture on that device.  Every call shares the one array:
-// the kernel leaves its arrival counters at zero, and each call clears them again on its
-// stream before launching; calls whose kernels overlap on the GPU (different streams running
-// concurrently on the same device) race on the scratch and must be serialized by the caller.
+// that address.  Make that first call before any stream capture on the device.  A __device__
+// array starts zero-filled when the module loads, and nothing here fills it in bulk: before
+// every launch the call clears the scratch's header (error word and arrival counters) with a
+// cudaMemsetAsync on the caller's own stream, so the clear is ordered with the kernel whatever
+// kind of stream the caller uses; the partials behind the header are always written before
+// they are read.  Every call shares the one array: calls whose kernels overlap on the GPU
+// (different streams running concurrently on the same device) race on the scratch and must be
+// serialized by the caller.  A bounded device-side wait that gives up leaves a non-zero error
+// word, which b2d_paged_decode_attn_noalloc_error reports until the next call clears it.
 #include <mutex>
 
 #include "common.cuh"
@@ -38,7 +42,7 @@ static constexpr int kMaxDevices = 64;
 static void* g_scratch_ptr[kMaxDevices] = {};
 static std::mutex g_scratch_mu;
 
-// Device address of the scratch array on the current device (set up on first use).
+// Device address of the scratch array on the current device (looked up on first use).
 static int scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -52,12 +56,7 @@ static int scratch_for_current_device(void** out) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_attn_scratch);
     if (e != cudaSuccess || p == nullptr) {
-      set_cuda_error(e);
-      return B2D_ERR_CUDA;
-    }
-    e = cudaMemset(p, 0, kNoAllocScratchBytes);
-    if (e != cudaSuccess) {
-      set_cuda_error(e);
+      set_cuda_error(e == cudaSuccess ? cudaErrorInvalidSymbol : e);
       return B2D_ERR_CUDA;
     }
     g_scratch_ptr[dev] = p;
@@ -94,6 +93,20 @@ int b2d_paged_decode_attn_noalloc(void* qkv, int qkv_dtype, int ldqkv, uint16_t*
                            n_blocks, ctx_lens, inv_freq, n_heads, n_kv_heads, head_dim, batch,
                            max_ctx, scale, window, append, out, out_dtype, ldout, scratch,
                            kNoAllocScratchBytes, s);
+}
+
+int b2d_paged_decode_attn_noalloc_error(void) {
+  void* scratch = nullptr;
+  B2D_TRY(scratch_for_current_device(&scratch));
+  // the last call may run on any stream of this device: wait for all of them
+  cudaError_t e = cudaDeviceSynchronize();
+  int word = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    return B2D_ERR_CUDA;
+  }
+  return word ? B2D_ERR_TIMEOUT : B2D_OK;
 }
 
 }  // extern "C"

@@ -146,6 +146,7 @@ int add_f32(float* x, const float* p, size_t n, cudaStream_t stream) {
 
 // Residual add + RMSNorm to fp16 (the tensor-core GEMMs' activation operand), one CTA per row:
 //   if p: x += p (written back);   out = fp16(x * rsqrt(mean(x^2) + eps) * gamma)
+// and, with out_lo, the remainder fp16(v - out) into out_lo (the B2D_F16X2 lo plane).
 // (rmsnorm LK/kernels.metal:71-89; the add is the residual update after a tensor-parallel
 // all-reduce).  Launched with programmatic dependent launch.
 // Row width handled from registers: up to kNormVec float4 per thread (D <= 4096 at 256 threads);
@@ -164,16 +165,18 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 
 __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const float* p,
                                                               const float* gamma, float eps,
-                                                              uint16_t* out, int D) {
+                                                              uint16_t* out, uint16_t* out_lo,
+                                                              int D) {
   __shared__ float red[8];
   pdl_wait();
   float* xr = x + (size_t)blockIdx.x * D;
   const float* pr = p ? p + (size_t)blockIdx.x * D : nullptr;
   uint16_t* orow = out + (size_t)blockIdx.x * D;
+  uint16_t* lrow = out_lo ? out_lo + (size_t)blockIdx.x * D : nullptr;
   const bool vec = (D & 3) == 0 && D <= kNormVec * 4 * 256 &&
                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gamma) |
                      reinterpret_cast<uintptr_t>(p)) & 15) == 0 &&
-                   (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+                   ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(out_lo)) & 7) == 0;
   if (vec) {
     // all loads of the row issued before the first use: one memory latency, not D/256 of them
     float4 v[kNormVec];
@@ -207,10 +210,10 @@ __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const fl
       const int i = threadIdx.x + k * 256;
       if (4 * i < D) {
         const float4 g = reinterpret_cast<const float4*>(gamma)[i];
-        const __half2 lo = __floats2half2_rn(v[k].x * scale * g.x, v[k].y * scale * g.y);
-        const __half2 hi = __floats2half2_rn(v[k].z * scale * g.z, v[k].w * scale * g.w);
-        reinterpret_cast<uint2*>(orow)[i] =
-            make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        uint2 lo;
+        reinterpret_cast<uint2*>(orow)[i] = split4_f16(v[k].x * scale * g.x, v[k].y * scale * g.y,
+                                                       v[k].z * scale * g.z, v[k].w * scale * g.w, &lo);
+        if (lrow) reinterpret_cast<uint2*>(lrow)[i] = lo;
       }
     }
     return;
@@ -226,29 +229,32 @@ __global__ void __launch_bounds__(256) add_rmsnorm_f16_kernel(float* x, const fl
   }
   const float scale = rsqrtf(block_sum_256(ss, red) / (float)D + eps);
   pdl_launch_dependents();
-  for (int i = threadIdx.x; i < D; i += 256) orow[i] = f2h(xr[i] * scale * gamma[i]);
+  for (int i = threadIdx.x; i < D; i += 256) store_f16_split(orow, lrow, i, xr[i] * scale * gamma[i]);
 }
 
 int add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps, uint16_t* out,
-                    int rows, int D, cudaStream_t stream) {
+                    uint16_t* out_lo, int rows, int D, cudaStream_t stream) {
   if (!x || !gamma || !out) return B2D_ERR_NULL;
   if (rows <= 0 || D <= 0) return B2D_ERR_SHAPE;
   return launch_pdl(add_rmsnorm_f16_kernel, dim3(rows), dim3(256), 0, stream, x, p, gamma, eps,
-                    out, D);
+                    out, out_lo, D);
 }
 
 // Embedding gather + RMSNorm to fp16: x[b] = float(E[tokens[b]]); out[b] = fp16(norm(x[b])*gamma)
-// (embed LK/kernels.metal:31-39 fused with the first layer's rmsnorm).
+// (embed LK/kernels.metal:31-39 fused with the first layer's rmsnorm); with out_lo, also the
+// B2D_F16X2 lo plane.
 __global__ void __launch_bounds__(256) embed_rmsnorm_f16_kernel(const uint16_t* E,
                                                                 const int* tokens, float* x,
                                                                 const float* gamma, float eps,
-                                                                uint16_t* out, int D) {
+                                                                uint16_t* out, uint16_t* out_lo,
+                                                                int D) {
   __shared__ float red[8];
   pdl_wait();
   const size_t tok = (size_t)tokens[blockIdx.x];
   const uint16_t* er = E + tok * D;
   float* xr = x + (size_t)blockIdx.x * D;
   uint16_t* orow = out + (size_t)blockIdx.x * D;
+  uint16_t* lrow = out_lo ? out_lo + (size_t)blockIdx.x * D : nullptr;
   float ss = 0.f;
   for (int i = threadIdx.x; i < D; i += 256) {
     const float v = h2f(er[i]);
@@ -262,15 +268,16 @@ __global__ void __launch_bounds__(256) embed_rmsnorm_f16_kernel(const uint16_t* 
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float scale = rsqrtf(tot / (float)D + eps);
   pdl_launch_dependents();
-  for (int i = threadIdx.x; i < D; i += 256) orow[i] = f2h(xr[i] * scale * gamma[i]);
+  for (int i = threadIdx.x; i < D; i += 256) store_f16_split(orow, lrow, i, xr[i] * scale * gamma[i]);
 }
 
 int embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
-                      float eps, uint16_t* out, int D, int batch, cudaStream_t stream) {
+                      float eps, uint16_t* out, uint16_t* out_lo, int D, int batch,
+                      cudaStream_t stream) {
   if (!E || !tokens || !x || !gamma || !out) return B2D_ERR_NULL;
   if (D <= 0 || batch <= 0) return B2D_ERR_SHAPE;
   return launch_pdl(embed_rmsnorm_f16_kernel, dim3(batch), dim3(256), 0, stream, E, tokens, x,
-                    gamma, eps, out, D);
+                    gamma, eps, out, out_lo, D);
 }
 
 }  // namespace b2d

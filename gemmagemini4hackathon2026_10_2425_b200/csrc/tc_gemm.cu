@@ -2,6 +2,14 @@
 //
 //   Y[b, m] = epilogue( sum_k W[m, k] * X[b, k] ),  b < batch <= 32,  W fp16 [M, K], X fp16 [batch, K]
 //
+// Activations at fp32 precision (XS = 2): the reference multiplies fp16 weights by fp32
+// activations (LK/kernels.metal:106-131).  An fp32 activation x is carried as two fp16 planes,
+// hi = fp16(x) and lo = fp16(x - hi) (~22 significant bits); both planes are loaded into one B
+// tile of 2N rows, so a single tcgen05.mma with N doubled produces W*hi and W*lo side by side in
+// TMEM, and the epilogue adds the two columns of each token.  fp16 x fp16 products are exact
+// and accumulate in fp32, so the result is the fp32-activation product.  The extra MMA columns
+// cost no weight bytes (the tensor pipe is a few percent busy at decode batch sizes).
+//
 // Why tensor cores here: at batch 16-32 a decode GEMV does 32-64 flops per weight byte; keeping
 // up with ~6.5 TB/s of HBM needs 200-400 TFLOP/s, beyond the CUDA cores' fp32 FMA rate.  The
 // reference runs these projections as matvec_f16 / matvec_gate_up_silu (LK/kernels.metal:106-173)
@@ -45,12 +53,14 @@ constexpr int kMaxSplits = 8;  // K splits of a row tile = CTAs of one (portable
 struct Params {
   CUtensorMap tmA;   // W      [M, K] fp16, box {64, 128}, 128B swizzle
   CUtensorMap tmA2;  // W_up   (SwiGLU only)
-  CUtensorMap tmB;   // X      [batch, K] fp16, box {64, N}, 128B swizzle
+  CUtensorMap tmB;   // X      [batch, K] fp16, box {64, N}, 128B swizzle (the hi plane for XS=2)
+  CUtensorMap tmB2;  // X lo plane [batch, K] (XS = 2 only)
   int M, K, batch;
   int k_tiles, k_splits, m_tiles;
   int epi;           // B2D_EPI_*
   void* y;
   int y_f16;
+  void* y_lo;        // fp16 output as hi/lo planes: lo = fp16(v - hi) here (nullptr: hi only)
   int ldy;
   const float* aux;
   int* err;                  // error word
@@ -80,10 +90,21 @@ __device__ __forceinline__ void store_y(const P& p, size_t yi, float v) {
     for (int i = 0; i < 8; ++i)
       if (i < p.n_ys) p.ys[i][yi] = v;
   } else if (p.y_f16) {
-    reinterpret_cast<uint16_t*>(p.y)[yi] = f2h(v);
+    const uint16_t hi = f2h(v);
+    reinterpret_cast<uint16_t*>(p.y)[yi] = hi;
+    if (p.y_lo) reinterpret_cast<uint16_t*>(p.y_lo)[yi] = f2h(v - h2f(hi));
   } else {
     reinterpret_cast<float*>(p.y)[yi] = v;
   }
+}
+
+// Previous value of y[yi] (ADD epilogue): fp32, fp16, or the hi + lo fp16 planes.
+template <typename P>
+__device__ __forceinline__ float load_y(const P& p, size_t yi) {
+  if (!p.y_f16) return reinterpret_cast<const float*>(p.y)[yi];
+  float v = h2f(reinterpret_cast<const uint16_t*>(p.y)[yi]);
+  if (p.y_lo) v += h2f(reinterpret_cast<const uint16_t*>(p.y_lo)[yi]);
+  return v;
 }
 
 // (value, row) -> 64-bit key whose unsigned order is "larger value, then lower row": the high
@@ -179,9 +200,13 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) {
   tmem_ld<16>(taddr + 16, v + 16);
 }
 
-// Weight-ring depth (stages of 64 K-columns) of the fp16 kernels.
+// Weight-ring depth (stages of 64 K-columns) of the fp16 kernels.  With hi/lo activation planes
+// (XS = 2) a single-matrix stage is 24 KB instead of 20 KB: 3 stages keep two CTAs per SM.
 #ifndef B2D_TC_STAGES
 #define B2D_TC_STAGES 4
+#endif
+#ifndef B2D_TC_STAGES_X2
+#define B2D_TC_STAGES_X2 3
 #endif
 #ifndef B2D_TC_STAGES_DUAL
 #define B2D_TC_STAGES_DUAL 4
@@ -191,16 +216,18 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, float* v) {
 // streams the raw tiles; four dequant warps expand them into the fp16 operand).
 constexpr int threads_for(int quant) { return quant ? 192 : 128; }
 
-template <int N, bool DUAL, int QUANT = 0>
+template <int N, bool DUAL, int QUANT = 0, int XS = 1>
 struct Cfg {
+  static constexpr int NB = N * XS;                    // MMA N: tokens x activation planes
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-  static constexpr int B_BYTES = N * BK * 2;           // 2 / 4 KB
+  static constexpr int B_BYTES = NB * BK * 2;          // 2 / 4 KB per plane
   static constexpr int B_OFF = A_BYTES * (DUAL ? 2 : 1);
   // fp16 weights: one ring of STAGES x [A | (A_up) | B], filled by TMA
   static constexpr int STAGE_BYTES = B_OFF + B_BYTES;
   // non-dual: 4 stages (~100 KB) so two CTAs share an SM and one streams while the other
   // runs its prologue or epilogue; dual (gate/up, 36 KB stages): one CTA per SM
-  static constexpr int STAGES = DUAL ? B2D_TC_STAGES_DUAL : B2D_TC_STAGES;
+  static constexpr int STAGES =
+      DUAL ? B2D_TC_STAGES_DUAL : (XS == 2 ? B2D_TC_STAGES_X2 : B2D_TC_STAGES);
   // quantized weights: a deep ring of RS raw tiles (the HBM stream) and a shallow ring of AS
   // operand stages [A fp16 | B] that the dequant warps fill
   static constexpr int RAW_ROW = QUANT == 1 ? BK : (QUANT == 2 ? BK / 2 : 0);  // bytes per row
@@ -216,13 +243,17 @@ struct Cfg {
   // 16-byte reads of consecutive rows fall in distinct banks); ks x (BM / ks) = BM rows in all
   static constexpr int RED_FLOATS = NACC * BM * (N + 4);
   static constexpr int SMEM = RING_BYTES + RED_FLOATS * 4 + 1024;  // + alignment slack
-  static constexpr uint32_t TMEM_COLS = (N * NACC <= 32) ? 32 : 64;
+  static constexpr int ACC_COLS = NB * NACC;  // TMEM columns the accumulators use
+  static constexpr uint32_t TMEM_COLS = ACC_COLS <= 32 ? 32 : (ACC_COLS <= 64 ? 64 : 128);
+  // CTAs of this kernel one SM holds (228 KB of shared memory per SM, ~1 KB reserved per CTA,
+  // plus the kernel's static shared memory)
+  static constexpr int CTAS_PER_SM = 2 * (SMEM + 4096) <= 228 * 1024 ? 2 : 1;
 };
 
-template <int N, bool DUAL, bool ARGMAX, int QUANT = 0>
+template <int N, bool DUAL, bool ARGMAX, int QUANT = 0, int XS = 1>
 __global__ void __launch_bounds__(threads_for(QUANT), 1)
     tc_gemm_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<N, DUAL, QUANT>;
+  using C = Cfg<N, DUAL, QUANT, XS>;
   constexpr int EPI0 = QUANT ? 2 : 0;  // first epilogue warp (epilogue warps hold TMEM quarters)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -312,6 +343,9 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         mbar_expect_tx(&a_full[as], C::B_BYTES);
         tma_load_2d(smem + as * C::STAGE_BYTES + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0,
                     &a_full[as]);
+        if constexpr (XS == 2)  // lo plane: rows N..2N-1 of the B tile
+          tma_load_2d(smem + as * C::STAGE_BYTES + C::B_OFF + N * BK * 2, &p.tmB2,
+                      (kt_begin + i) * BK, 0, &a_full[as]);
         const int j = i + C::RS;  // raw tile that reuses the slot k-tile i is draining
         if (j < nkt) {
           const int rs = i % C::RS;
@@ -328,6 +362,8 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       for (int i = 0; i < first; ++i) {
         uint8_t* st = smem + i * C::STAGE_BYTES;
         tma_load_2d(st + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[i]);
+        if constexpr (XS == 2)
+          tma_load_2d(st + C::B_OFF + N * BK * 2, &p.tmB2, (kt_begin + i) * BK, 0, &full_bar[i]);
       }
       for (int i = first; i < nkt; ++i) {
         const int s = i % C::STAGES;
@@ -341,11 +377,13 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         if (DUAL)
           load_a_tile(st + C::A_BYTES, &p.tmA2, p.pA2, m_tile, p.k_tiles, kt_begin + i, &full_bar[s]);
         tma_load_2d(st + C::B_OFF, &p.tmB, (kt_begin + i) * BK, 0, &full_bar[s]);
+        if constexpr (XS == 2)
+          tma_load_2d(st + C::B_OFF + N * BK * 2, &p.tmB2, (kt_begin + i) * BK, 0, &full_bar[s]);
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
-    const uint32_t idesc = idesc_f16<N>();
+    const uint32_t idesc = idesc_f16<C::NB>();
     bool ok = true;
     for (int i = 0; i < nkt; ++i) {
       const int s = QUANT ? i % C::AS : i % C::STAGES;
@@ -365,7 +403,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         mma_f16(tmem, a + 2 * k, b + 2 * k, idesc, acc);
         if (DUAL) {
           const uint64_t a2 = smem_desc_sw128(st + C::A_BYTES);
-          mma_f16(tmem + N, a2 + 2 * k, b + 2 * k, idesc, acc);
+          mma_f16(tmem + C::NB, a2 + 2 * k, b + 2 * k, idesc, acc);
         }
       }
       mma_commit(QUANT ? &a_empty[s] : &empty_bar[s]);  // slot free once these MMAs read it
@@ -480,7 +518,18 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   if (have && epi_warp) {
     const uint32_t taddr = tmem + (uint32_t((warp & 3) * 32) << 16);
     tmem_ld<N>(taddr, acc);
-    if (DUAL) tmem_ld<N>(taddr + N, acc2);
+    if (DUAL) tmem_ld<N>(taddr + C::NB, acc2);
+    if constexpr (XS == 2) {  // add the lo-plane columns of each token
+      float lo[N];
+      tmem_ld<N>(taddr + N, lo);
+#pragma unroll
+      for (int t = 0; t < N; ++t) acc[t] += lo[t];
+      if constexpr (DUAL) {
+        tmem_ld<N>(taddr + C::NB + N, lo);
+#pragma unroll
+        for (int t = 0; t < N; ++t) acc2[t] += lo[t];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -530,7 +579,8 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     pdl_wait();
     pdl_launch_dependents();
     const int nq = own_rows * (N / 4);
-    if (!DUAL && ok && epi_warp && (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL)) {
+    if (!DUAL && ok && epi_warp &&
+        (p.epi == B2D_EPI_ADD || p.epi == B2D_EPI_GELU_MUL || p.epi == B2D_EPI_SILU_MUL)) {
 #pragma unroll
       for (int k = 0; k < MAXQ; ++k) {
         const int v = etid + k * THREADS;
@@ -541,10 +591,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
           yv[k][j] = 0.f;
           if (v < nq && t0 + j < p.batch && grow < p.M) {
             const size_t yi = (size_t)(t0 + j) * p.ldy + grow;
-            yv[k][j] = p.epi == B2D_EPI_GELU_MUL
-                           ? p.aux[yi]
-                           : (p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
-                                      : reinterpret_cast<const float*>(p.y)[yi]);
+            yv[k][j] = p.epi == B2D_EPI_ADD ? load_y(p, yi) : p.aux[yi];
           }
         }
       }
@@ -586,6 +633,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             y = av[j];
             if (p.epi == B2D_EPI_ADD) y += yv[k][j];
             else if (p.epi == B2D_EPI_GELU_MUL) y = gelu_tanh(y) * yv[k][j];
+            else if (p.epi == B2D_EPI_SILU_MUL) y = silu(y) * yv[k][j];
           }
           store_y(p, yi, y);
         }
@@ -648,10 +696,11 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       } else {
         v = acc[t];
         if (p.epi == B2D_EPI_ADD)
-          v += p.y_f16 ? h2f(reinterpret_cast<const uint16_t*>(p.y)[yi])
-                       : reinterpret_cast<const float*>(p.y)[yi];
+          v += load_y(p, yi);
         else if (p.epi == B2D_EPI_GELU_MUL)
           v = gelu_tanh(v) * p.aux[yi];
+        else if (p.epi == B2D_EPI_SILU_MUL)
+          v = silu(v) * p.aux[yi];
       }
       store_y(p, yi, v);
     }
@@ -742,10 +791,10 @@ size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue) {
   return tc_plan(M, K, batch, epilogue).total;
 }
 
-template <int N, bool DUAL, bool ARGMAX, int QUANT = 0>
+template <int N, bool DUAL, bool ARGMAX, int QUANT = 0, int XS = 1>
 static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
-  using C = tc::Cfg<N, DUAL, QUANT>;
-  auto kern = tc::tc_gemm_kernel<N, DUAL, ARGMAX, QUANT>;
+  using C = tc::Cfg<N, DUAL, QUANT, XS>;
+  auto kern = tc::tc_gemm_kernel<N, DUAL, ARGMAX, QUANT, XS>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -787,7 +836,7 @@ static int launch_tc(const tc::Params& prm, dim3 grid, cudaStream_t stream) {
 // K splits (= cluster size) for a row-tile count: the largest power of two <= 8 whose clusters
 // all fit on the GPU in one wave (cudaOccupancyMaxActiveClusters for this kernel), without
 // more CTAs than SMs and without splitting K below one 64-wide tile.
-template <int N, bool DUAL, int QUANT = 0>
+template <int N, bool DUAL, int QUANT = 0, int XS = 1>
 static int tc_pick_splits(int m_tiles, int k_tiles) {
   // The largest power-of-two split (<= 8, the portable cluster size) whose CTAs all fit on the
   // SMs at once: two per SM for the single-matrix fp16 kernel (about 100 KB of shared memory;
@@ -798,7 +847,9 @@ static int tc_pick_splits(int m_tiles, int k_tiles) {
 #ifndef B2D_TC_SPLIT_CTAS_PER_SM
 #define B2D_TC_SPLIT_CTAS_PER_SM 2
 #endif
-  const int slots = (!DUAL && !QUANT ? B2D_TC_SPLIT_CTAS_PER_SM : 1) * num_sms();
+  using C = tc::Cfg<N, DUAL, QUANT, XS>;
+  const int per_sm = !DUAL && !QUANT ? std::min(B2D_TC_SPLIT_CTAS_PER_SM, C::CTAS_PER_SM) : 1;
+  const int slots = per_sm * num_sms();
   for (int ks = 8; ks >= 2; ks >>= 1)
     if (ks <= k_tiles && m_tiles * ks <= slots) return ks;
   return 1;
@@ -812,21 +863,44 @@ struct TcCall {
   int n_tile;
   bool dual, argmax;
   int quant = 0;  // 0 fp16, 1 q8_32, 2 q4_32
+  int xs = 1;     // activation planes: 1 fp16, 2 hi + lo fp16
 };
 
-int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
-                    int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
-                    int K, int batch, float* logits, int* tokens, float* max_vals,
-                    int index_offset, void* workspace, size_t workspace_bytes,
+// Split count for a call's kernel variant.
+static int pick_splits(int n_tile, bool dual, int quant, int xs, int m_tiles, int k_tiles) {
+#define B2D_PICK(NT, DU, QU, X)                          \
+  if (n_tile == NT && dual == DU && quant == QU && xs == X) \
+    return tc_pick_splits<NT, DU, QU, X>(m_tiles, k_tiles);
+#define B2D_PICK_Q(NT, DU, X) B2D_PICK(NT, DU, 0, X) B2D_PICK(NT, DU, 1, X) B2D_PICK(NT, DU, 2, X)
+  B2D_PICK_Q(16, false, 1)
+  B2D_PICK_Q(16, false, 2)
+  B2D_PICK_Q(32, false, 1)
+  B2D_PICK_Q(32, false, 2)
+  B2D_PICK(16, true, 0, 1)
+  B2D_PICK(16, true, 0, 2)
+  B2D_PICK(32, true, 0, 1)
+  B2D_PICK(32, true, 0, 2)
+#undef B2D_PICK_Q
+#undef B2D_PICK
+  return 1;
+}
+
+// x_dtype B2D_F16 (X fp16 [batch, ldx]) or B2D_F16X2 (hi plane X, lo plane X + batch * ldx);
+// y_dtype B2D_F32, B2D_F16 or B2D_F16X2 (lo plane y + batch * ldy).
+int tc_gemm_prepare(TcCall* call, int x_dtype, const uint16_t* W, const uint16_t* W_up,
+                    const uint16_t* X, int ldx, int epilogue, int y_dtype, void* y, int ldy,
+                    const float* aux, int M, int K, int batch, float* logits, int* tokens,
+                    float* max_vals, int index_offset, void* workspace, size_t workspace_bytes,
                     bool packed = false, float* const* ys = nullptr, int n_ys = 0) {
   if (!call || !W || !X) return B2D_ERR_NULL;
+  if (x_dtype != B2D_F16 && x_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
   if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 8 || ldx < K || ldx % 8 ||
       M > kMaxTiles * tc::BM)
     return B2D_ERR_SHAPE;
-  if (epilogue < B2D_EPI_STORE || epilogue > B2D_EPI_ARGMAX) return B2D_ERR_UNSUPPORTED;
-  if (y_dtype != B2D_F32 && y_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
+  if (epilogue < B2D_EPI_STORE || epilogue > B2D_EPI_SILU_MUL) return B2D_ERR_UNSUPPORTED;
+  if (y_dtype != B2D_F32 && y_dtype != B2D_F16 && y_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
   if (epilogue == B2D_EPI_SWIGLU && !W_up) return B2D_ERR_NULL;
-  if (epilogue == B2D_EPI_GELU_MUL && !aux) return B2D_ERR_NULL;
+  if ((epilogue == B2D_EPI_GELU_MUL || epilogue == B2D_EPI_SILU_MUL) && !aux) return B2D_ERR_NULL;
   if (epilogue == B2D_EPI_ARGMAX && !tokens) return B2D_ERR_NULL;
   if (epilogue != B2D_EPI_ARGMAX && !y && n_ys == 0) return B2D_ERR_NULL;
   if (n_ys < 0 || n_ys > 8 || (n_ys > 0 && (!ys || epilogue != B2D_EPI_STORE || y_dtype != B2D_F32)))
@@ -845,7 +919,9 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
     B2D_TRY(make_tmap_f16(&p.tmA, W, M, K, K, tc::BM));
     if (W_up) B2D_TRY(make_tmap_f16(&p.tmA2, W_up, M, K, K, tc::BM));
   }
+  const int xs = x_dtype == B2D_F16X2 ? 2 : 1;
   B2D_TRY(make_tmap_f16(&p.tmB, X, batch, K, ldx, pl.n_tile));
+  if (xs == 2) B2D_TRY(make_tmap_f16(&p.tmB2, X + (size_t)batch * ldx, batch, K, ldx, pl.n_tile));
   char* ws = static_cast<char*>(workspace);
   p.M = M;
   p.K = K;
@@ -855,7 +931,8 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
   p.m_tiles = pl.m_tiles;
   p.epi = epilogue;
   p.y = y;
-  p.y_f16 = y_dtype == B2D_F16;
+  p.y_f16 = y_dtype != B2D_F32;
+  p.y_lo = (y_dtype == B2D_F16X2 && y) ? static_cast<uint16_t*>(y) + (size_t)batch * ldy : nullptr;
   p.ldy = epilogue == B2D_EPI_ARGMAX ? M : ldy;
   p.aux = aux;
   p.err = reinterpret_cast<int*>(ws);
@@ -870,56 +947,59 @@ int tc_gemm_prepare(TcCall* call, const uint16_t* W, const uint16_t* W_up, const
     if (!ys[i]) return B2D_ERR_NULL;
     p.ys[i] = ys[i];
   }
-  if (epilogue != B2D_EPI_ARGMAX) {
-    const bool dual = epilogue == B2D_EPI_SWIGLU;
-    p.k_splits = pl.n_tile == 16 ? (dual ? tc_pick_splits<16, true>(pl.m_tiles, pl.k_tiles)
-                                         : tc_pick_splits<16, false>(pl.m_tiles, pl.k_tiles))
-                                 : (dual ? tc_pick_splits<32, true>(pl.m_tiles, pl.k_tiles)
-                                         : tc_pick_splits<32, false>(pl.m_tiles, pl.k_tiles));
-  }
+  if (epilogue != B2D_EPI_ARGMAX)
+    p.k_splits = pick_splits(pl.n_tile, epilogue == B2D_EPI_SWIGLU, 0, xs, pl.m_tiles, pl.k_tiles);
   call->grid = dim3(pl.m_tiles, p.k_splits);
   call->n_tile = pl.n_tile;
   call->dual = epilogue == B2D_EPI_SWIGLU;
   call->argmax = epilogue == B2D_EPI_ARGMAX;
+  call->quant = 0;
+  call->xs = xs;
   return B2D_OK;
 }
 
-int tc_gemm_launch(const TcCall& c, cudaStream_t stream) {
+template <int XS>
+static int tc_gemm_launch_xs(const TcCall& c, cudaStream_t stream) {
   if (c.quant == 1)
-    return c.n_tile == 16 ? launch_tc<16, false, false, 1>(c.prm, c.grid, stream)
-                          : launch_tc<32, false, false, 1>(c.prm, c.grid, stream);
+    return c.n_tile == 16 ? launch_tc<16, false, false, 1, XS>(c.prm, c.grid, stream)
+                          : launch_tc<32, false, false, 1, XS>(c.prm, c.grid, stream);
   if (c.quant == 2)
-    return c.n_tile == 16 ? launch_tc<16, false, false, 2>(c.prm, c.grid, stream)
-                          : launch_tc<32, false, false, 2>(c.prm, c.grid, stream);
+    return c.n_tile == 16 ? launch_tc<16, false, false, 2, XS>(c.prm, c.grid, stream)
+                          : launch_tc<32, false, false, 2, XS>(c.prm, c.grid, stream);
   if (c.n_tile == 16) {
-    if (c.argmax) return launch_tc<16, false, true>(c.prm, c.grid, stream);
-    if (c.dual) return launch_tc<16, true, false>(c.prm, c.grid, stream);
-    return launch_tc<16, false, false>(c.prm, c.grid, stream);
+    if (c.argmax) return launch_tc<16, false, true, 0, XS>(c.prm, c.grid, stream);
+    if (c.dual) return launch_tc<16, true, false, 0, XS>(c.prm, c.grid, stream);
+    return launch_tc<16, false, false, 0, XS>(c.prm, c.grid, stream);
   }
-  if (c.argmax) return launch_tc<32, false, true>(c.prm, c.grid, stream);
-  if (c.dual) return launch_tc<32, true, false>(c.prm, c.grid, stream);
-  return launch_tc<32, false, false>(c.prm, c.grid, stream);
+  if (c.argmax) return launch_tc<32, false, true, 0, XS>(c.prm, c.grid, stream);
+  if (c.dual) return launch_tc<32, true, false, 0, XS>(c.prm, c.grid, stream);
+  return launch_tc<32, false, false, 0, XS>(c.prm, c.grid, stream);
 }
 
-int tc_gemm(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx, int epilogue,
-            int y_dtype, void* y, int ldy, const float* aux, int M, int K, int batch,
-            float* logits, int* tokens, float* max_vals, int index_offset, void* workspace,
-            size_t workspace_bytes, cudaStream_t stream) {
+int tc_gemm_launch(const TcCall& c, cudaStream_t stream) {
+  return c.xs == 2 ? tc_gemm_launch_xs<2>(c, stream) : tc_gemm_launch_xs<1>(c, stream);
+}
+
+int tc_gemm(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
+            int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
+            int batch, float* logits, int* tokens, float* max_vals, int index_offset,
+            void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   TcCall c;
-  B2D_TRY(tc_gemm_prepare(&c, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch,
-                          logits, tokens, max_vals, index_offset, workspace, workspace_bytes));
+  B2D_TRY(tc_gemm_prepare(&c, x_dtype, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
+                          batch, logits, tokens, max_vals, index_offset, workspace,
+                          workspace_bytes));
   return tc_gemm_launch(c, stream);
 }
 
 // STORE of the fp32 product into n_ys copies (row stride ldy each), e.g. every tensor-parallel
 // rank's receive buffer.
-int tc_gemm_multi_store(const uint16_t* W, const uint16_t* X, int ldx, float* const* ys, int n_ys,
-                        int ldy, int M, int K, int batch, void* workspace, size_t workspace_bytes,
-                        cudaStream_t stream) {
+int tc_gemm_multi_store(int x_dtype, const uint16_t* W, const uint16_t* X, int ldx,
+                        float* const* ys, int n_ys, int ldy, int M, int K, int batch,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   TcCall c;
-  B2D_TRY(tc_gemm_prepare(&c, W, nullptr, X, ldx, B2D_EPI_STORE, B2D_F32, nullptr, ldy, nullptr, M,
-                          K, batch, nullptr, nullptr, nullptr, 0, workspace, workspace_bytes, false,
-                          ys, n_ys));
+  B2D_TRY(tc_gemm_prepare(&c, x_dtype, W, nullptr, X, ldx, B2D_EPI_STORE, B2D_F32, nullptr, ldy,
+                          nullptr, M, K, batch, nullptr, nullptr, nullptr, 0, workspace,
+                          workspace_bytes, false, ys, n_ys));
   return tc_gemm_launch(c, stream);
 }
 
@@ -929,7 +1009,7 @@ int tc_gemm_packed(const uint8_t* Wp, const uint8_t* Wp_up, const uint16_t* X, i
                    int batch, float* logits, int* tokens, float* max_vals, int index_offset,
                    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   TcCall c;
-  B2D_TRY(tc_gemm_prepare(&c, reinterpret_cast<const uint16_t*>(Wp),
+  B2D_TRY(tc_gemm_prepare(&c, B2D_F16, reinterpret_cast<const uint16_t*>(Wp),
                           reinterpret_cast<const uint16_t*>(Wp_up), X, ldx, epilogue, y_dtype, y,
                           ldy, aux, M, K, batch, logits, tokens, max_vals, index_offset,
                           workspace, workspace_bytes, true));
@@ -977,15 +1057,20 @@ int tc_pack_f16(const uint16_t* W, int ldw, int M, int K, void* out, cudaStream_
 }
 
 // Quantized weights (q8_32 / q4_32) on the tensor cores: STORE / ADD / GELU_MUL epilogues.
-int tc_gemm_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X, int ldx,
-              int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
-              int batch, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
-  if (!q || !scales || !X || !y) return B2D_ERR_NULL;
+int tc_gemm_q(int x_dtype, int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X,
+              int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+              int K, int batch, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+              float* const* ys, int n_ys) {
+  if (!q || !scales || !X || (!y && n_ys == 0)) return B2D_ERR_NULL;
   if (w_dtype != B2D_Q8_32 && w_dtype != B2D_Q4_32) return B2D_ERR_UNSUPPORTED;
-  if (epilogue != B2D_EPI_STORE && epilogue != B2D_EPI_ADD && epilogue != B2D_EPI_GELU_MUL)
+  if (x_dtype != B2D_F16 && x_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
+  if (n_ys < 0 || n_ys > 8 || (n_ys > 0 && (!ys || epilogue != B2D_EPI_STORE || y_dtype != B2D_F32)))
     return B2D_ERR_UNSUPPORTED;
-  if (y_dtype != B2D_F32 && y_dtype != B2D_F16) return B2D_ERR_UNSUPPORTED;
-  if (epilogue == B2D_EPI_GELU_MUL && !aux) return B2D_ERR_NULL;
+  if (epilogue != B2D_EPI_STORE && epilogue != B2D_EPI_ADD && epilogue != B2D_EPI_GELU_MUL &&
+      epilogue != B2D_EPI_SILU_MUL)
+    return B2D_ERR_UNSUPPORTED;
+  if (y_dtype != B2D_F32 && y_dtype != B2D_F16 && y_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
+  if ((epilogue == B2D_EPI_GELU_MUL || epilogue == B2D_EPI_SILU_MUL) && !aux) return B2D_ERR_NULL;
   if (M <= 0 || K <= 0 || batch <= 0 || batch > 32 || K % 32 || ldx < K || ldx % 8 || ldy < M ||
       M > kMaxTiles * tc::BM)
     return B2D_ERR_SHAPE;
@@ -999,8 +1084,10 @@ int tc_gemm_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t
   tc::Params& p = c.prm;
   p = tc::Params{};
   const int row_bytes = quant == 1 ? K : K / 2;
+  const int xs = x_dtype == B2D_F16X2 ? 2 : 1;
   B2D_TRY(make_tmap_u8(&p.tmA, q, M, row_bytes, quant == 1 ? tc::BK : tc::BK / 2, tc::BM));
   B2D_TRY(make_tmap_f16(&p.tmB, X, batch, K, ldx, pl.n_tile));
+  if (xs == 2) B2D_TRY(make_tmap_f16(&p.tmB2, X + (size_t)batch * ldx, batch, K, ldx, pl.n_tile));
   char* ws = static_cast<char*>(workspace);
   p.M = M;
   p.K = K;
@@ -1009,22 +1096,25 @@ int tc_gemm_q(int w_dtype, const void* q, const uint16_t* scales, const uint16_t
   p.m_tiles = pl.m_tiles;
   p.epi = epilogue;
   p.y = y;
-  p.y_f16 = y_dtype == B2D_F16;
+  p.y_f16 = y_dtype != B2D_F32;
+  p.y_lo = (y_dtype == B2D_F16X2 && y) ? static_cast<uint16_t*>(y) + (size_t)batch * ldy : nullptr;
   p.ldy = ldy;
   p.aux = aux;
   p.err = reinterpret_cast<int*>(ws);
   p.am_counter = reinterpret_cast<unsigned int*>(ws + 64);
   p.scales = scales;
-  p.k_splits = pl.n_tile == 16
-                   ? (quant == 1 ? tc_pick_splits<16, false, 1>(pl.m_tiles, pl.k_tiles)
-                                 : tc_pick_splits<16, false, 2>(pl.m_tiles, pl.k_tiles))
-                   : (quant == 1 ? tc_pick_splits<32, false, 1>(pl.m_tiles, pl.k_tiles)
-                                 : tc_pick_splits<32, false, 2>(pl.m_tiles, pl.k_tiles));
+  p.n_ys = n_ys;
+  for (int i = 0; i < n_ys; ++i) {
+    if (!ys[i]) return B2D_ERR_NULL;
+    p.ys[i] = ys[i];
+  }
+  p.k_splits = pick_splits(pl.n_tile, false, quant, xs, pl.m_tiles, pl.k_tiles);
   c.grid = dim3(pl.m_tiles, p.k_splits);
   c.n_tile = pl.n_tile;
   c.dual = false;
   c.argmax = false;
   c.quant = quant;
+  c.xs = xs;
   return tc_gemm_launch(c, stream);
 }
 

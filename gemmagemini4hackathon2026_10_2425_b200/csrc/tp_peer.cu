@@ -52,24 +52,27 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
 // Per-slot barrier among the tp ranks.  Thread r < tp announces this rank to rank r and then
 // waits for rank r's announcement.  The data a rank announces was written by the previous kernel
-// on that rank (its partial in its own memory, or pushed into the peers' receive slots): that
-// grid has completed -- its stores, remote ones included, are performed -- before this kernel
-// passes griddepcontrol.wait and writes the flag, so the flag needs no release fence, and the
-// readers fetch the data with L1-bypassing loads after the wait and a CTA barrier.  System-scope
-// fences cost ~9 us per launch here (measured), which is why they are avoided.  Returns false
-// (CTA-uniform) if some peer did not arrive within timeout_ns; *err then holds B2D_ERR_TIMEOUT.
+// on that rank (its partial in its own memory, or pushed into the peers' receive slots); that
+// grid completed before this kernel passed griddepcontrol.wait, so those writes precede the
+// announcement in causality order.  The announcement is a release store at system scope and the
+// poll an acquire load at system scope: a peer that observes the epoch therefore observes the
+// data too (PTX memory model, release/acquire pattern across GPUs), and the CTA barrier that
+// follows carries that to every thread of the reader's CTA, whose loads bypass L1.  Only the
+// flag word is released / acquired (one thread per peer), not a full system-scope fence.
+// Returns false (CTA-uniform) if some peer did not arrive within timeout_ns; *err then holds
+// B2D_ERR_TIMEOUT.
 __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, uint32_t* epochs,
                              long long timeout_ns, int* err) {
   __shared__ uint32_t epoch_s;
@@ -83,11 +86,11 @@ __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, u
   bool ok = true;
   if (threadIdx.x < tp) {
     const int r = threadIdx.x;
-    st_relaxed_sys(sig[r] + slot * kSigStride + rank, e);
+    st_release_sys(sig[r] + slot * kSigStride + rank, e);
     const uint32_t* mine = sig[rank] + slot * kSigStride + r;
-    if ((int)(ld_volatile(mine) - e) < 0) {
+    if ((int)(ld_acquire_sys(mine) - e) < 0) {
       const uint64_t t0 = global_ns();
-      while ((int)(ld_volatile(mine) - e) < 0) {
+      while ((int)(ld_acquire_sys(mine) - e) < 0) {
         if ((long long)(global_ns() - t0) > timeout_ns) {
           ok = false;
           atomicExch(err, B2D_ERR_TIMEOUT);
@@ -95,7 +98,6 @@ __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, u
         }
       }
     }
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
   }
   return __syncthreads_and(ok) != 0;
 }
@@ -103,7 +105,8 @@ __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, u
 // x[b] += sum_r part_r[b]; out16[b] = fp16(rmsnorm(x[b]) * gamma) if gamma (else x only).
 __global__ void __launch_bounds__(256) tp_allreduce_add_rmsnorm_kernel(
     const __grid_constant__ PeerSet ps, uint32_t* epochs, int rank, int tp, int slot0, float* x,
-    const float* gamma, float eps, uint16_t* out16, int D, long long timeout_ns, int* err) {
+    const float* gamma, float eps, uint16_t* out16, uint16_t* out_lo, int D,
+    long long timeout_ns, int* err) {
   __shared__ float red[8];
   pdl_wait();  // this rank's partial and residual are complete
   const int b = blockIdx.x;
@@ -142,12 +145,14 @@ __global__ void __launch_bounds__(256) tp_allreduce_add_rmsnorm_kernel(
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
   const float scale = rsqrtf(tot / (float)D + eps);
   uint2* orow = reinterpret_cast<uint2*>(out16 + (size_t)b * D);
+  uint2* lrow = out_lo ? reinterpret_cast<uint2*>(out_lo + (size_t)b * D) : nullptr;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
   for (int i = threadIdx.x; i < n4; i += blockDim.x) {
     const float4 xv = xr[i], g = g4[i];
-    __half2 lo = __floats2half2_rn(xv.x * scale * g.x, xv.y * scale * g.y);
-    __half2 hi = __floats2half2_rn(xv.z * scale * g.z, xv.w * scale * g.w);
-    orow[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    uint2 lo;
+    orow[i] = split4_f16(xv.x * scale * g.x, xv.y * scale * g.y, xv.z * scale * g.z,
+                         xv.w * scale * g.w, &lo);
+    if (lrow) lrow[i] = lo;  // B2D_F16X2 lo plane
   }
 }
 
@@ -175,8 +180,8 @@ __global__ void __launch_bounds__(128) tp_argmax_gather_kernel(
 
 int tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs, uint32_t* epochs,
                              int rank, int tp, int slot0, float* x, const float* gamma,
-                             float eps, uint16_t* out16, int D, int rows, long long timeout_ns,
-                             int* err, cudaStream_t stream) {
+                             float eps, uint16_t* out16, uint16_t* out_lo, int D, int rows,
+                             long long timeout_ns, int* err, cudaStream_t stream) {
   if (!parts || !sigs || !epochs || !x || !err) return B2D_ERR_NULL;
   if (tp < 1 || tp > kMaxTp || rank < 0 || rank >= tp || rows <= 0 || D <= 0 || D % 4 ||
       slot0 < 0 || timeout_ns <= 0)
@@ -189,10 +194,12 @@ int tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs, u
     ps.part[r] = parts[r];
     ps.sig[r] = sigs[r];
   }
-  if (!aligned16(x) || (gamma && (!aligned16(gamma) || (reinterpret_cast<uintptr_t>(out16) & 7))))
+  if (!aligned16(x) ||
+      (gamma && (!aligned16(gamma) ||
+                 ((reinterpret_cast<uintptr_t>(out16) | reinterpret_cast<uintptr_t>(out_lo)) & 7))))
     return B2D_ERR_ALIGN;
   return launch_pdl(tp_allreduce_add_rmsnorm_kernel, dim3(rows), dim3(256), 0, stream, ps,
-                    epochs, rank, tp, slot0, x, gamma, eps, out16, D, timeout_ns, err);
+                    epochs, rank, tp, slot0, x, gamma, eps, out16, out_lo, D, timeout_ns, err);
 }
 
 int tp_argmax_gather(const float* const* vals, const int* const* idxs, uint32_t* const* sigs,

@@ -116,32 +116,56 @@ class DecodeEngine:
             self.k_pages.append(k)
             self.v_pages.append(v)
 
-    def load_weights(self, w: dict[str, torch.Tensor]) -> None:
+    def load_weights(self, w: dict[str, torch.Tensor], quant: dict[str, str] | None = None) -> None:
         """Full (unsharded) weights -> this rank's shards on the device, registered with the
-        library.  Needs alloc_kv() first."""
+        library.  Needs alloc_kv() first.  `quant` maps matrix names to "q8_32" / "q4_32" for
+        projections stored quantized (w[name] the integers, w[name + ".scales"] the fp16 block
+        scales); a layer's five projections then share one format and stay quantized on the
+        device (b2d_decoder_set_layer_q)."""
         if not self.k_pages:
             raise RuntimeError("alloc_kv() before load_weights()")
         s, dev = self.shape, self.device
+        quant = quant or {}
         self.layers = []
+        names = ("attn_norm", "wqkv", "wo", "ffn_norm", "wgate", "wup", "wdown")
+        mats = ("wqkv", "wo", "wgate", "wup", "wdown")
         for i in range(s.n_layers):
-            full = {n: w[f"l{i}.{n}"] for n in ("attn_norm", "wqkv", "wo", "ffn_norm", "wgate", "wup", "wdown")}
-            sh = {k: v.to(dev) for k, v in tpmod.shard_layer(full, s, self.rank, self.tp).items()}
+            fmts = {quant.get(f"l{i}.{n}") for n in mats}
+            if len(fmts) != 1:
+                raise ValueError(f"layer {i}: all five projections must share one weight format, got {sorted(map(str, fmts))}")
+            fmt = fmts.pop()
+            full = {n: w[f"l{i}.{n}"] for n in names}
+            if fmt is None:
+                sh = {k: v.to(dev) for k, v in tpmod.shard_layer(full, s, self.rank, self.tp).items()}
+                for k in mats:
+                    sh[k] = sh[k].half().contiguous()
+            else:
+                full.update({f"{n}.scales": w[f"l{i}.{n}.scales"] for n in mats})
+                sh = {k: v.to(dev) for k, v in tpmod.shard_layer_quant(full, s, self.rank, self.tp, fmt).items()}
+                for k in mats:
+                    sh[k + ".scales"] = sh[k + ".scales"].half().contiguous()
             sh["attn_norm"] = sh["attn_norm"].float().contiguous()
             sh["ffn_norm"] = sh["ffn_norm"].float().contiguous()
-            for k in ("wqkv", "wo", "wgate", "wup", "wdown"):
-                sh[k] = sh[k].half().contiguous()
             self.layers.append(sh)
+            code = {None: _lib.F16, "q8_32": _lib.Q8_32, "q4_32": _lib.Q4_32}[fmt]
+            sc = (lambda k: None) if fmt is None else (lambda k: sh[k + ".scales"].data_ptr())
             call(
-                "b2d_decoder_set_layer",
+                "b2d_decoder_set_layer_q",
                 self._h,
                 i,
+                code,
                 sh["attn_norm"].data_ptr(),
                 sh["wqkv"].data_ptr(),
+                sc("wqkv"),
                 sh["wo"].data_ptr(),
+                sc("wo"),
                 sh["ffn_norm"].data_ptr(),
                 sh["wgate"].data_ptr(),
+                sc("wgate"),
                 sh["wup"].data_ptr(),
+                sc("wup"),
                 sh["wdown"].data_ptr(),
+                sc("wdown"),
                 self.k_pages[i].data_ptr(),
                 self.v_pages[i].data_ptr(),
             )
@@ -165,9 +189,11 @@ class DecodeEngine:
         a = np.ascontiguousarray(np.asarray(inv_freq, dtype=np.float32))
         call("b2d_decoder_set_inv_freq", self._h, a.ctypes.data, a.size)
 
-    def load_weights_file(self, path) -> dict:
+    def load_weights_file(self, path, dequantize: bool = False) -> dict:
         """Load a weights file in the reference's format (weights.py) into this rank's shards
-        and apply its RoPE settings; returns the file's config.  Needs alloc_kv() first."""
+        and apply its RoPE settings; returns the file's config.  Needs alloc_kv() first.
+        Projections stored quantized stay quantized on the device (the decode step streams
+        them as stored); dequantize=True expands them to fp16(scale * q) instead."""
         from . import weights as W
 
         wf = W.read_weights(path)
@@ -177,13 +203,18 @@ class DecodeEngine:
         import numpy as np
 
         # the mapped file is read-only: each tensor is copied once on its way to the device
-        self.load_weights({k: torch.from_numpy(np.array(v)) for k, v in W.tensors_for_engine(wf).items()})
+        t = W.tensors_for_engine(wf, keep_quant=not dequantize)
+        self.load_weights({k: torch.from_numpy(np.array(v)) for k, v in t.items()}, None if dequantize else wf.quant)
         self.set_inv_freq(W.inv_freq_from_config(wf.config))
         return wf.config
 
-    def random_weights(self, seed: int, std: float = 0.02) -> None:
+    def random_weights(self, seed: int, std: float = 0.02, quant: str | None = None) -> None:
         """Seeded random-init weights generated on the device (fp16 ~ N(0, std), norms = 1).
-        Every rank draws the same full matrices and keeps its shard."""
+        Every rank draws the same full matrices and keeps its shard.  quant ("q8_32" /
+        "q4_32") stores the five projections of every layer in that 32-block format instead,
+        quantized from the same fp16 draws (weights.quantize_torch)."""
+        from . import weights as W
+
         s, dev = self.shape, self.device
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
@@ -192,6 +223,7 @@ class DecodeEngine:
             return (torch.randn(m, k, generator=g, device=dev, dtype=torch.float32) * std).half()
 
         w = {"embed": mat(s.vocab, s.dim), "final_norm": torch.ones(s.dim, device=dev)}
+        qmap = {}
         for i in range(s.n_layers):
             w[f"l{i}.attn_norm"] = torch.ones(s.dim, device=dev)
             w[f"l{i}.wqkv"] = mat(s.qkv_dim, s.dim)
@@ -200,8 +232,12 @@ class DecodeEngine:
             w[f"l{i}.wgate"] = mat(s.ffn_dim, s.dim)
             w[f"l{i}.wup"] = mat(s.ffn_dim, s.dim)
             w[f"l{i}.wdown"] = mat(s.dim, s.ffn_dim)
-            # shard layer by layer so the full model never sits on the device at once
-        self.load_weights(w)
+            if quant:
+                for n in ("wqkv", "wo", "wgate", "wup", "wdown"):
+                    name = f"l{i}.{n}"
+                    w[name], w[name + ".scales"] = W.quantize_torch(w[name], quant)
+                    qmap[name] = quant
+        self.load_weights(w, qmap or None)
         del w
         torch.cuda.empty_cache()
 

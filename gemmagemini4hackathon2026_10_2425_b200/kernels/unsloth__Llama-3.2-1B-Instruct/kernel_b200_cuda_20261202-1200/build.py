@@ -1,9 +1,8 @@
 #!/usr/bin/env python3
 """Build step of the kernel folder: compiles libb200dec.so (sm_100a) in-tree."""
-import sys
-from pathlib import Path
+from _repo import add_package_to_path
 
-sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+add_package_to_path()
 from gemmagemini4hackathon2026_10_2425_b200.build import build  # noqa: E402
 
 print(build())

@@ -9,11 +9,11 @@ this script re-writes or validates such a file with gemmagemini4hackathon2026_10
                                              projections as 32-block int8 / 4-bit + fp16 scales
 """
 import argparse
-import sys
-from pathlib import Path
 
-sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
-import numpy as np  # noqa: E402
+import numpy as np
+from _repo import add_package_to_path
+
+add_package_to_path()
 
 from gemmagemini4hackathon2026_10_2425_b200 import weights as W  # noqa: E402
 

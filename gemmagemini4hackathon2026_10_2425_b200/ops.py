@@ -294,6 +294,21 @@ def rope_kv_append(qkv, k_pages, v_pages, block_table, ctx_lens, inv_freq_dev, n
     )
 
 
+def to_f16x2(x: torch.Tensor) -> torch.Tensor:
+    """fp32 [B, K] -> the B2D_F16X2 form fp16 [2, B, K]: hi = fp16(x), lo = fp16(x - hi)."""
+    hi = x.to(torch.float16)
+    return torch.stack([hi, (x - hi.float()).to(torch.float16)])
+
+
+def from_f16x2(t: torch.Tensor) -> torch.Tensor:
+    """fp16 [2, B, K] hi + lo planes -> fp32 [B, K]."""
+    return t[0].float() + t[1].float()
+
+
+def _is_x2(t: torch.Tensor | None) -> bool:
+    return t is not None and t.dim() == 3 and t.shape[0] == 2 and t.dtype == torch.float16
+
+
 def attn_workspace_bytes(batch, n_heads, n_kv_heads, head_dim, max_ctx) -> int:
     return int(_lib.lib().b2d_paged_attn_workspace_bytes(batch, n_heads, n_kv_heads, head_dim, max_ctx))
 
@@ -317,10 +332,12 @@ def paged_decode_attn(
     out_dtype: torch.dtype = torch.float32,
     workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Ragged paged decode attention; see include/b200dec.h b2d_paged_decode_attn."""
+    """Ragged paged decode attention; see include/b200dec.h b2d_paged_decode_attn.  `out` may be
+    fp16 [2, B, Hq*HD]: the output as B2D_F16X2 hi + lo planes."""
     B = qkv.shape[0]
     if out is None:
         out = torch.empty(B, n_heads * head_dim, dtype=out_dtype, device=qkv.device)
+    out_dt = _lib.F16X2 if _is_x2(out) else _DT[out.dtype]
     nbytes = attn_workspace_bytes(B, n_heads, n_kv_heads, head_dim, max_ctx)
     ws = workspace if workspace is not None else _WS_ATTN.get(nbytes, qkv.device)
     _need_cuda(qkv, k_pages, v_pages, block_table, ctx_lens, inv_freq_dev, out, ws)
@@ -347,8 +364,8 @@ def paged_decode_attn(
         int(window),
         1 if append else 0,
         out.data_ptr(),
-        _DT[out.dtype],
-        out.shape[1],
+        out_dt,
+        out.shape[-1],
         ws.data_ptr(),
         ws.numel(),
         _stream(),
@@ -357,7 +374,7 @@ def paged_decode_attn(
 
 
 _WS_TC = Workspace()
-_TC_EPI = {"store": _lib.EPI_STORE, "add": _lib.EPI_ADD, "gelu_mul": _lib.EPI_GELU_MUL, "swiglu": _lib.EPI_SWIGLU, "argmax": _lib.EPI_ARGMAX}
+_TC_EPI = {"store": _lib.EPI_STORE, "add": _lib.EPI_ADD, "gelu_mul": _lib.EPI_GELU_MUL, "swiglu": _lib.EPI_SWIGLU, "argmax": _lib.EPI_ARGMAX, "silu_mul": _lib.EPI_SILU_MUL}
 
 
 @dataclass
@@ -403,15 +420,19 @@ def gemm_tc(
     workspace: torch.Tensor | None = None,
 ):
     """Tensor-core batched GEMV (tcgen05): y[b] = epilogue(W @ X[b]) for fp16 W [M, K] and fp16
-    X [batch <= 32, K].  For 'argmax' returns tokens (and logits if asked).  W (and W_up) may
-    be row-major or packed by pack_tc."""
+    X [batch <= 32, K], or X fp16 [2, batch, K]: fp32-precision activations as B2D_F16X2 hi + lo
+    planes (to_f16x2).  y may be fp16 [2, batch, M] (B2D_F16X2 output) as well.  For 'argmax'
+    returns tokens (and logits if asked).  W (and W_up) may be row-major or packed by pack_tc."""
     M, K = W.shape
-    B = X.shape[0]
+    x2 = _is_x2(X)
+    B = X.shape[-2]
     packed = isinstance(W, TcPacked)
     if packed != (W_up is None or isinstance(W_up, TcPacked)) and W_up is not None:
         raise ValueError("W and W_up must both be packed or both row-major")
-    if (not packed and W.dtype != torch.float16) or X.dtype != torch.float16 or X.shape[1] != K:
-        raise ValueError("gemm_tc needs fp16 W [M, K] and fp16 X [batch, K]")
+    if (not packed and W.dtype != torch.float16) or X.dtype != torch.float16 or X.shape[-1] != K:
+        raise ValueError("gemm_tc needs fp16 W [M, K] and fp16 X [batch, K] (or [2, batch, K])")
+    if packed and x2:
+        raise ValueError("hi/lo activations run on row-major weights")
     Wt = W.buf if packed else W
     Wu = (W_up.buf if packed else W_up) if W_up is not None else None
     ws = workspace if workspace is not None else _WS_TC.get(tc_workspace_bytes(M, K, B, epilogue), X.device)
@@ -425,12 +446,17 @@ def gemm_tc(
             if epilogue == "add":
                 raise ValueError("epilogue 'add' needs y")
             y = torch.empty(B, M, dtype=out_dtype, device=X.device)
-        if y.dtype not in _DT or tuple(y.shape) != (B, M):
-            raise ValueError(f"y must be fp32/fp16 [{B}, {M}]")
-        ydt = _DT[y.dtype]
+        if _is_x2(y) and tuple(y.shape) == (2, B, M):
+            ydt = _lib.F16X2
+        elif y.dtype in _DT and tuple(y.shape) == (B, M):
+            ydt = _DT[y.dtype]
+        else:
+            raise ValueError(f"y must be fp32/fp16 [{B}, {M}] or fp16 [2, {B}, {M}]")
     _need_cuda(Wt, X, Wu, aux, y, ws, tokens, logits)
+    head = () if packed else (_lib.F16X2 if x2 else _lib.F16,)
     call(
-        "b2d_gemm_tc_packed" if packed else "b2d_gemm_tc",
+        "b2d_gemm_tc_packed" if packed else "b2d_gemm_tc_ex",
+        *head,
         Wt.data_ptr(),
         _ptr(Wu),
         X.data_ptr(),
@@ -467,13 +493,14 @@ def gemm_tc_q(
     workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Tensor-core batched GEMV over 32-block quantized weights: y[b] = epilogue(W @ X[b]) with
-    W = scale * q dequantized in shared memory to fp16 (the MMA operand), fp16 X [batch <= 32, K].
-    Epilogues 'store', 'add', 'gelu_mul'."""
+    W = scale * q dequantized in shared memory to fp16 (the MMA operand), fp16 X [batch <= 32, K]
+    or hi + lo planes fp16 [2, batch, K].  Epilogues 'store', 'add', 'gelu_mul'."""
     M, K = Wq.shape
-    B = X.shape[0]
-    if X.dtype != torch.float16 or X.shape[1] != K:
-        raise ValueError("gemm_tc_q needs fp16 X [batch, K]")
-    if epilogue not in ("store", "add", "gelu_mul"):
+    x2 = _is_x2(X)
+    B = X.shape[-2]
+    if X.dtype != torch.float16 or X.shape[-1] != K:
+        raise ValueError("gemm_tc_q needs fp16 X [batch, K] (or [2, batch, K])")
+    if epilogue not in ("store", "add", "gelu_mul", "silu_mul"):
         raise ValueError(f"gemm_tc_q: unsupported epilogue {epilogue!r}")
     ws = workspace if workspace is not None else _WS_TC.get(tc_workspace_bytes(M, K, B, epilogue), X.device)
     if y is None:
@@ -484,7 +511,8 @@ def gemm_tc_q(
         raise ValueError(f"y must be fp32/fp16 [{B}, {M}]")
     _need_cuda(Wq.q, Wq.scales, X, aux, y, ws)
     call(
-        "b2d_gemm_tc_q",
+        "b2d_gemm_tc_q_ex",
+        _lib.F16X2 if x2 else _lib.F16,
         Wq.dtype_code,
         Wq.q.data_ptr(),
         Wq.scales.data_ptr(),
@@ -584,9 +612,13 @@ def tp_argmax_gather(
     return tokens
 
 
-def add_rmsnorm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float, p: torch.Tensor | None = None) -> torch.Tensor:
-    """x += p (if given, in place); returns fp16 rmsnorm(x) * gamma."""
-    out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+def add_rmsnorm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float, p: torch.Tensor | None = None, x2: bool = False) -> torch.Tensor:
+    """x += p (if given, in place); returns fp16 rmsnorm(x) * gamma, or with x2 the B2D_F16X2
+    hi + lo planes fp16 [2, rows, D]."""
+    out = torch.empty(((2,) if x2 else ()) + tuple(x.shape), dtype=torch.float16, device=x.device)
     _need_cuda(x, gamma, p)
-    call("b2d_add_rmsnorm_f16", x.data_ptr(), _ptr(p), gamma.data_ptr(), float(eps), out.data_ptr(), x.shape[0], x.shape[1], _stream())
+    call(
+        "b2d_add_rmsnorm", x.data_ptr(), _ptr(p), gamma.data_ptr(), float(eps), _lib.F16X2 if x2 else _lib.F16,
+        out.data_ptr(), x.shape[0], x.shape[1], _stream(),
+    )
     return out

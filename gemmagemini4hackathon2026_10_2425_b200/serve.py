@@ -3,7 +3,8 @@
 The reference's Python side drives a model through a kernel folder (kernel.json + a `binary`) that
 speaks a JSON-lines protocol on stdin/stdout (IK/surfaces/DESIGN_AND_LIMITATIONS.md:70-88;
 implemented by LK/main.swift:494-622, driven by IK/surfaces/runners/kernel_runner.py:20-96).
-This module is that binary for the CUDA path; `kernel_folder/llm` runs its main().  Same flags:
+This module is that binary for the CUDA path; the `llm` of the package's kernel folder
+(kernels/unsloth__Llama-3.2-1B-Instruct/kernel_b200_cuda_20261202-1200/) runs its main().  Same flags:
 
     --weights PATH --max-ctx N --serve
     --prompt-ids a,b,c --gen N [--dump-logits PATH]
@@ -22,6 +23,14 @@ One sequence at a time (batch 1), greedy, every request from an empty cache.  Th
 prefilled in chunks of 32 consecutive positions per step (b2d_decoder_prefill: tcgen05
 projections, each chunk's K/V written before its rows attend); --no-gemm prefills one token per
 decode step, as the reference's --no-gemm does.
+
+Generation never waits for the host between steps: each step is one launch of the device-
+resident loop (b2d_decoder_generate: step + next token fed back + position advanced, all on the
+GPU), up to WINDOW steps are in flight, and the host reads each token from pinned memory once its
+step's event has completed -- the reference's window of command buffers in flight
+(LK/main.swift:473-491).  A stop token seen on the host ends the request; the steps already in
+flight past it only write cache positions the next request overwrites.  --bench-tg times n steps
+launched back to back with one synchronization at the end (LK/main.swift:374-381, 605-618).
 """
 
 from __future__ import annotations
@@ -73,6 +82,7 @@ def parse_request(line: str, vocab: int, max_ctx: int) -> tuple[list[int], int, 
 
 
 PREFILL_CHUNK = 32  # positions per prefill step (the tcgen05 projections take up to 32 rows)
+WINDOW = 3  # decode steps in flight while streaming (the reference keeps 3 command buffers queued)
 
 
 class Session:
@@ -102,6 +112,12 @@ class Session:
         self.logits = torch.empty(1, self.eng.lm_rows, dtype=torch.float32, device=dev)
         self.h_in = torch.zeros(2, dtype=torch.int32).pin_memory()
         self.h_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+        # device-resident loop: a ring of generated tokens, copied to pinned host slots
+        self.ring_len = 4 * WINDOW
+        self.ring = torch.zeros(self.ring_len, 1, **i32)
+        self.ring_count = torch.zeros(1, **i32)
+        self.h_ring = torch.zeros(self.ring_len, dtype=torch.int32).pin_memory()
+        self.events = [torch.cuda.Event() for _ in range(self.ring_len)]
         self.device_name = torch.cuda.get_device_name(dev)
 
     @property
@@ -142,6 +158,55 @@ class Session:
     def last_logits(self):
         return self.logits[0].float().cpu().numpy()
 
+    def _start(self, token_dev_or_host, pos: int) -> None:
+        """Set the loop's input token (a host int, or None: the prefill's next token already on
+        the device) and position; resets the ring count."""
+        s = self.eng.stream
+        with self.torch.cuda.stream(s):
+            if token_dev_or_host is None:
+                self.tok.copy_(self.nxt)
+            else:
+                self.h_in[0] = int(token_dev_or_host)
+                self.tok.copy_(self.h_in[0:1], non_blocking=True)
+            self.h_in[1] = pos
+            self.pos.copy_(self.h_in[1:2], non_blocking=True)
+            self.ring_count.zero_()
+
+    def _launch(self, k: int) -> None:
+        """Enqueue loop step k (the k-th since _start): one step + advance, then the token's copy
+        into pinned host slot k % ring_len and an event that marks it readable."""
+        s = self.eng.stream
+        slot = k % self.ring_len
+        with self.torch.cuda.stream(s):
+            self.eng.generate(self.tok, self.pos, self.table, 1, self.ring, self.ring_count)
+            self.h_ring[slot : slot + 1].copy_(self.ring[slot], non_blocking=True)
+            self.events[slot].record(s)
+
+    def _token(self, k: int) -> int:
+        slot = k % self.ring_len
+        self.events[slot].synchronize()
+        return int(self.h_ring[slot])
+
+    def generate(self, first: int | None, pos: int, n: int):
+        """Yield up to n tokens following `first` (host int, or None after prefill: the device's
+        next token) at position pos, with up to WINDOW steps in flight.  The caller may stop
+        early; steps already enqueued then just finish."""
+        self._start(first, pos)
+        launched = 0
+        for k in range(n):
+            while launched < min(k + WINDOW, n):
+                self._launch(launched)
+                launched += 1
+            yield self._token(k)
+
+    def run_steps(self, first: int, pos: int, n: int) -> None:
+        """n loop steps back to back from token `first` at `pos`, one synchronization at the end."""
+        self._start(first, pos)
+        s = self.eng.stream
+        with self.torch.cuda.stream(s):
+            self.eng.generate(self.tok, self.pos, self.table, n, self.ring, self.ring_count)
+        s.synchronize()
+
 
 def _emit(obj: dict, out) -> None:
     out.write(json.dumps(obj) + "\n")
@@ -151,6 +216,7 @@ def _emit(obj: dict, out) -> None:
 def serve(sess: Session, inp=sys.stdin, out=sys.stdout) -> None:
     sess.prefill([BOS % sess.vocab] * 2)  # warm-up: graph capture, first launches
     sess.step(0, 2)
+    list(sess.generate(None, 3, 2))
     _emit({"ready": True, "max_ctx": sess.max_ctx, "vocab": sess.vocab, "device": sess.device_name}, out)
     for line in inp:
         if not line.strip():
@@ -164,7 +230,8 @@ def serve(sess: Session, inp=sys.stdin, out=sys.stdout) -> None:
         tok = sess.prefill(ids)
         t_prefill = time.perf_counter() - t0
         t1 = time.perf_counter()
-        produced, finish, pos = 0, "length", len(ids)
+        produced, finish = 0, "length"
+        following = sess.generate(None, len(ids), max_tokens - 1)
         while produced < max_tokens:
             if tok in stop:
                 finish = "stop"
@@ -173,8 +240,8 @@ def serve(sess: Session, inp=sys.stdin, out=sys.stdout) -> None:
             produced += 1
             if produced >= max_tokens:
                 break
-            tok = sess.step(tok, pos)
-            pos += 1
+            tok = next(following)
+        following.close()
         _emit(
             {
                 "done": True,
@@ -208,8 +275,7 @@ def main(argv=None) -> int:
             sess.last_logits().astype("<f4").tofile(a.dump_logits)
         toks = [tok]
         t1 = time.perf_counter()
-        for k in range(1, a.gen):
-            toks.append(sess.step(toks[-1], len(ids) + k - 1))
+        toks += list(sess.generate(None, len(ids), max(a.gen - 1, 0)))
         t_dec = time.perf_counter() - t1
         print(json.dumps({
             "tokens": toks[: a.gen],
@@ -236,9 +302,7 @@ def main(argv=None) -> int:
             bos = BOS % s.vocab
 
             def run():
-                t = bos
-                for p in range(n):
-                    t = sess.step(t, p)
+                sess.run_steps(bos, 0, n)
 
             run()
             rates = []

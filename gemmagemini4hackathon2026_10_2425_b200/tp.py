@@ -78,6 +78,35 @@ def shard_layer(w: dict[str, torch.Tensor], shape: ModelShape, rank: int, tp: in
     }
 
 
+def shard_layer_quant(
+    w: dict[str, torch.Tensor], shape: ModelShape, rank: int, tp: int, fmt: str
+) -> dict[str, torch.Tensor]:
+    """shard_layer for a layer whose five projections are stored in the 32-block format `fmt`
+    ("q8_32": int8 [M, K]; "q4_32": uint8 [M, K/2], two elements per byte), each with
+    `<name>.scales` fp16 [M, K/32].  Column-parallel matrices split their rows (integers and
+    scales alike); row-parallel ones split K, which must stay a multiple of 32 per rank."""
+    check_tp(shape, tp)
+    hd, hq, f = shape.head_dim, shape.n_heads // tp, shape.ffn_dim // tp
+    per_byte = 2 if fmt == "q4_32" else 1
+    rows = qkv_rows(shape, rank, tp).to(w["wqkv"].device)
+
+    def cols(name: str, a: int, b: int) -> tuple[torch.Tensor, torch.Tensor]:
+        if a % 32 or b % 32:
+            raise ValueError(f"{name}: a rank's K range [{a}, {b}) must hold whole 32-element blocks")
+        q, sc = w[name], w[name + ".scales"]
+        return q[:, a // per_byte : b // per_byte].contiguous(), sc[:, a // 32 : b // 32].contiguous()
+
+    out = {"attn_norm": w["attn_norm"].contiguous(), "ffn_norm": w["ffn_norm"].contiguous()}
+    out["wqkv"] = w["wqkv"].index_select(0, rows).contiguous()
+    out["wqkv.scales"] = w["wqkv.scales"].index_select(0, rows).contiguous()
+    out["wo"], out["wo.scales"] = cols("wo", rank * hq * hd, (rank + 1) * hq * hd)
+    for n in ("wgate", "wup"):
+        out[n] = w[n][rank * f : (rank + 1) * f].contiguous()
+        out[n + ".scales"] = w[n + ".scales"][rank * f : (rank + 1) * f].contiguous()
+    out["wdown"], out["wdown.scales"] = cols("wdown", rank * f, (rank + 1) * f)
+    return out
+
+
 def shard_head(embed: torch.Tensor, shape: ModelShape, rank: int, tp: int) -> torch.Tensor:
     a, b = vocab_rows(shape, rank, tp)
     return embed[a:b].contiguous()

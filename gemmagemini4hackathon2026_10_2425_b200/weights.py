@@ -161,13 +161,16 @@ def inv_freq_from_config(cfg: dict) -> np.ndarray:
     return np.asarray(inv, dtype=np.float64).astype(np.float32)
 
 
-def tensors_for_engine(wf: WeightsFile) -> dict[str, np.ndarray]:
+def tensors_for_engine(wf: WeightsFile, keep_quant: bool = False) -> dict[str, np.ndarray]:
     """The file's tensors under the names DecodeEngine.load_weights takes (lm_head falls back to
-    the tied embedding).  Quantized matrices become fp16(scale * q) -- the operand the tcgen05
-    quantized GEMM feeds its MMA -- since the decode step's projections are fp16."""
+    the tied embedding).  With keep_quant, quantized matrices stay as stored (integers under the
+    plain name, `<name>.scales` beside them; wf.quant names their format) for the decode step's
+    quantized projections.  Without it they become fp16(scale * q), the fp16 operand the tcgen05
+    quantized GEMM feeds its MMA."""
     t = dict(wf.tensors)
-    for name, fmt in (wf.quant or {}).items():
-        t[name] = dequantize(t[name], t.pop(name + ".scales"), fmt).astype(np.float16)
+    if not keep_quant:
+        for name, fmt in (wf.quant or {}).items():
+            t[name] = dequantize(t[name], t.pop(name + ".scales"), fmt).astype(np.float16)
     if "lm_head" not in t:
         t["lm_head"] = t["embed"]
     return t
@@ -194,6 +197,28 @@ def quantize(w: np.ndarray, fmt: str) -> tuple[np.ndarray, np.ndarray]:
         q = np.where(s32 > 0, np.rint(blocks / s32), 0.0)
     q = np.clip(q, qmin, qmax).astype(np.int8).reshape(m, k)
     return (q if fmt == "q8_32" else pack_q4(q)), scales
+
+
+def quantize_torch(w, fmt: str):
+    """quantize() on a torch tensor (any device): the same absmax rule, so seeded synthetic
+    weights can be quantized where they are generated.  Returns (q, scales) as torch tensors."""
+    import torch
+
+    if fmt not in QUANT_FORMATS:
+        raise ValueError(f"unknown format {fmt!r}")
+    m, k = w.shape
+    if k % 32:
+        raise ValueError("K must be a multiple of 32")
+    qmax, qmin = (127, -127) if fmt == "q8_32" else (7, -8)
+    blocks = w.float().reshape(m, k // 32, 32)
+    scales = (blocks.abs().amax(dim=2) / qmax).half()
+    s32 = scales.float().unsqueeze(-1)
+    q = torch.where(s32 > 0, torch.round(blocks / torch.where(s32 > 0, s32, 1.0)), 0.0)
+    q = q.clamp(qmin, qmax).to(torch.int8).reshape(m, k)
+    if fmt == "q4_32":
+        n = (q.to(torch.int16) & 0xF).to(torch.uint8)
+        q = n[:, 0::2] | (n[:, 1::2] << 4)
+    return q.contiguous(), scales.contiguous()
 
 
 def pack_q4(q: np.ndarray) -> np.ndarray:

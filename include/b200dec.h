@@ -58,7 +58,12 @@ enum b2d_status {
   B2D_ERR_STATE = 9        /* handle used out of order (e.g. step before weights are set) */
 };
 
-enum b2d_dtype { B2D_F32 = 0, B2D_F16 = 1, B2D_Q8_32 = 2, B2D_Q4_32 = 3 };
+/* B2D_F16X2: an fp32 value carried as two fp16 planes, hi = fp16(v) and lo = fp16(v - hi)
+ * (~22 significant bits), the tensor-core operand form of fp32 activations.  A [rows, cols]
+ * array of this type with row stride ld is the hi plane [rows, ld] followed by the lo plane,
+ * which starts rows * ld elements after the first.  (Extension: the reference keeps its
+ * activations in fp32, LK/kernels.metal:106-131; this is how they reach fp16 tensor cores.) */
+enum b2d_dtype { B2D_F32 = 0, B2D_F16 = 1, B2D_Q8_32 = 2, B2D_Q4_32 = 3, B2D_F16X2 = 4 };
 
 /* GEMV epilogues (GK/kernels.metal:151-198 EPI 0/1/2; LK/kernels.metal:139-173; :307-345). */
 enum b2d_epilogue {
@@ -66,7 +71,9 @@ enum b2d_epilogue {
   B2D_EPI_ADD = 1,      /* y += W x          (residual add)       */
   B2D_EPI_GELU_MUL = 2, /* y = gelu_tanh(W x) * aux                */
   B2D_EPI_SWIGLU = 3,   /* y = silu(W x) * (W_up x)                */
-  B2D_EPI_ARGMAX = 4    /* logits = W x (optional), token = argmax */
+  B2D_EPI_ARGMAX = 4,   /* logits = W x (optional), token = argmax */
+  B2D_EPI_SILU_MUL = 5  /* y = silu(W x) * aux: the gate half of a SwiGLU whose up half was
+                           computed separately (tensor-core GEMMs only) */
 };
 
 B2D_API const char* b2d_status_string(int status);
@@ -160,6 +167,16 @@ B2D_API int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t*
                         int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
                         int batch, float* logits, int* tokens, float* max_vals, int index_offset,
                         void* workspace, size_t workspace_bytes, b2d_stream_t stream);
+/* b2d_gemm_tc with the activation type explicit: x_dtype B2D_F16 (as above) or B2D_F16X2 --
+ * fp32-precision activations as hi + lo fp16 planes (X, and X + batch * ldx), multiplied in one
+ * tcgen05.mma of twice the N (the reference's fp16 W x fp32 x, LK/kernels.metal:106-131).
+ * y_dtype may be B2D_F16X2 too (lo plane at y + batch * ldy): the SwiGLU output that feeds the
+ * down projection. */
+B2D_API int b2d_gemm_tc_ex(int x_dtype, const uint16_t* W, const uint16_t* W_up,
+                           const uint16_t* X, int ldx, int epilogue, int y_dtype, void* y, int ldy,
+                           const float* aux, int M, int K, int batch, float* logits, int* tokens,
+                           float* max_vals, int index_offset, void* workspace,
+                           size_t workspace_bytes, b2d_stream_t stream);
 
 /* Packed weight layout for the tensor-core GEMV (an HBM layout choice of this library; the
  * reference's weights file is row-major, LK/convert_weights.py:60-72): W [M, K] fp16 becomes
@@ -189,6 +206,11 @@ B2D_API int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, co
                           int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux,
                           int M, int K, int batch, void* workspace, size_t workspace_bytes,
                           b2d_stream_t stream);
+/* b2d_gemm_tc_q with x_dtype B2D_F16 or B2D_F16X2 (hi + lo planes, as b2d_gemm_tc_ex). */
+B2D_API int b2d_gemm_tc_q_ex(int x_dtype, int w_dtype, const void* q, const uint16_t* scales,
+                             const uint16_t* X, int ldx, int epilogue, int y_dtype, void* y,
+                             int ldy, const float* aux, int M, int K, int batch, void* workspace,
+                             size_t workspace_bytes, b2d_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------
  * Small ops of the decode step
@@ -216,6 +238,11 @@ B2D_API int b2d_argmax_combine(const float* vals, const int* idxs, int n_parts, 
  * (rmsnorm LK/kernels.metal:71-89.) */
 B2D_API int b2d_add_rmsnorm_f16(float* x, const float* p, const float* gamma, float eps,
                                 uint16_t* out, int rows, int D, b2d_stream_t stream);
+/* The same with the output type explicit: out_dtype B2D_F16 (as above) or B2D_F16X2 (hi plane
+ * out[rows, D], lo plane at out + rows * D): the fp32-precision operand of the tensor-core
+ * projections. */
+B2D_API int b2d_add_rmsnorm(float* x, const float* p, const float* gamma, float eps, int out_dtype,
+                            void* out, int rows, int D, b2d_stream_t stream);
 
 /* Embedding + RMSNorm: x[b] = float(E[tokens[b]]); out[b] = fp16(rmsnorm(x[b]) * gamma)
  * (embed LK/kernels.metal:31-39 fused with the first rmsnorm). */
@@ -254,7 +281,8 @@ B2D_API int b2d_rope_kv_append(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_
  * load; partial softmax states go to `workspace` and the last CTA of each (sequence, KV head)
  * merges them.  The workspace must be zero-filled before its first use; every call leaves its
  * arrival counters at zero again, so it can be reused by later calls on the same stream.
- * out[b, Hq*HD] (row stride ldout, out_dtype F32 or F16).  head_dim 64, 128 or 256; n_heads /
+ * out[b, Hq*HD] (row stride ldout, out_dtype F32, F16 or F16X2 -- lo plane at out + batch *
+ * ldout).  head_dim 64, 128 or 256; n_heads /
  * n_kv_heads in {1, 2, 4, 8}.  scale <= 0 means 1/sqrt(head_dim) (LK/main.swift:293).
  * max_ctx bounds every ctx_lens[b] + 1 and sizes the workspace; n_blocks is the page-pool
  * size: a block-table entry outside [0, n_blocks) is never dereferenced (its keys are
@@ -277,10 +305,15 @@ B2D_API int b2d_paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t*
  * inside this library (held on every GPU that loads it until exit).  Sizes whose
  * b2d_paged_attn_workspace_bytes exceed b2d_paged_decode_attn_noalloc_max_scratch_bytes()
  * return B2D_ERR_WORKSPACE.  The first call on a device looks up the array's device address
- * and zero-fills it synchronously, so make that first call before any stream capture.
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.  Each call
+ * clears the array's header (error word, arrival counters) on `stream` before its kernel.
  * All calls share the array: calls whose kernels overlap on the GPU race on it.  Never calls
- * cudaMalloc / cudaFree.  Other arguments and results as b2d_paged_decode_attn. */
+ * cudaMalloc / cudaFree.  Other arguments and results as b2d_paged_decode_attn.
+ * b2d_paged_decode_attn_noalloc_error waits for the device (cudaDeviceSynchronize) and returns
+ * B2D_ERR_TIMEOUT if a bounded device-side wait of the most recent call on the current device
+ * gave up (its output is then incomplete), else B2D_OK; the next call clears the word. */
 B2D_API size_t b2d_paged_decode_attn_noalloc_max_scratch_bytes(void);
+B2D_API int b2d_paged_decode_attn_noalloc_error(void);
 B2D_API int b2d_paged_decode_attn_noalloc(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages,
                                           uint16_t* v_pages, const int* block_table,
                                           int max_blocks, int n_blocks, const int* ctx_lens,
@@ -347,9 +380,11 @@ B2D_API int b2d_decoder_generate(b2d_decoder* h, int* tokens, int* ctx_lens, con
 B2D_API int b2d_decoder_set_inv_freq(b2d_decoder* h, const float* inv_freq_host, int n);
 /* 1 if the steps so far use the peer-memory collectives, 0 for NCCL (or tp_size == 1). */
 B2D_API int b2d_decoder_peer_collectives(const b2d_decoder* h);
-/* Device-side status of the steps enqueued so far (synchronizes with the device): 0, or
- * B2D_ERR_TIMEOUT if a peer barrier gave up waiting for another rank (bounded wait, 10 s).
- * Reading clears it. */
+/* Device-side status of the steps enqueued so far (cudaDeviceSynchronize, then reads the error
+ * words): 0, or B2D_ERR_TIMEOUT if a bounded device-side wait gave up -- a peer barrier waiting
+ * for another rank (10 s), or a TMA / mbarrier wait inside the attention or a tensor-core GEMM
+ * (about 2 s); the outputs of that step are then incomplete.  Reading clears the error words
+ * and resets the split-K arrival counters, so later steps start clean. */
 B2D_API int b2d_decoder_error(b2d_decoder* h);
 
 /* Weights of this rank's shard (fp16 matrices, fp32 norms), as b2d_shard_* in the Python
@@ -359,6 +394,23 @@ B2D_API int b2d_decoder_set_layer(b2d_decoder* h, int layer, const float* attn_n
                           const uint16_t* wqkv, const uint16_t* wo, const float* ffn_norm,
                           const uint16_t* wgate, const uint16_t* wup, const uint16_t* wdown,
                           uint16_t* k_pages, uint16_t* v_pages);
+/* b2d_decoder_set_layer with the five projections in one weight type: w_dtype B2D_F16 (as
+ * b2d_decoder_set_layer; scales ignored) or B2D_Q8_32 / B2D_Q4_32 (layouts at the top of this
+ * file; each matrix with its fp16 scales [rows, K/32]), streamed as stored -- 1.06 / 0.56 bytes
+ * per weight instead of 2.  Batches below 9 run them on the tensor-core GEMV (integers exact in
+ * fp16, the block scale applied to each block's fp32 result: exact dequantization); batches of
+ * 9 and more on the tcgen05 GEMM, whose MMA operand is fp16(scale * q) (one fp16 rounding of
+ * the dequantized weight), the gate/up SwiGLU as an up GEMM and a gate GEMM with the SILU_MUL
+ * epilogue.  Every projection's K (D, local heads * HD, local FFN rows) must be a multiple of
+ * 32.  (Extension: the reference's quantized weights are roadmap only,
+ * ios_kernels/PLAN.md:175-176,256.) */
+B2D_API int b2d_decoder_set_layer_q(b2d_decoder* h, int layer, int w_dtype, const float* attn_norm,
+                                    const void* wqkv, const uint16_t* wqkv_scales, const void* wo,
+                                    const uint16_t* wo_scales, const float* ffn_norm,
+                                    const void* wgate, const uint16_t* wgate_scales,
+                                    const void* wup, const uint16_t* wup_scales, const void* wdown,
+                                    const uint16_t* wdown_scales, uint16_t* k_pages,
+                                    uint16_t* v_pages);
 /* embed [V, D] fp16 (replicated); lm_head [ceil(V/tp), D] fp16 rows of this rank's vocab
  * shard (the tied embedding's rows); final_norm [D]. */
 B2D_API int b2d_decoder_set_head(b2d_decoder* h, const uint16_t* embed, const uint16_t* lm_head,

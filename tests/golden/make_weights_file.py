@@ -1,6 +1,9 @@
 """Generate the weights-file fixtures with the reference's own converter (run once; committed).
 
-    python tests/golden/make_weights_file.py
+    python tests/golden/make_weights_file.py --reference PATH_TO_REFERENCE_CHECKOUT
+
+(or set REFERENCE_ROOT); PATH_TO_REFERENCE_CHECKOUT is the root of the reference project, the
+directory that holds ios_kernels/.
 
 1. A tiny random Llama (HF transformers, Llama-3 RoPE scaling on) is saved as a HF snapshot
    (config.json + model.safetensors) under a temporary HOME.
@@ -17,6 +20,7 @@ tests.
 
 from __future__ import annotations
 
+import argparse
 import os
 import shutil
 import subprocess
@@ -29,9 +33,8 @@ import torch
 from transformers import LlamaConfig, LlamaForCausalLM
 
 HERE = Path(__file__).resolve().parent
-REF_CONVERTER = Path(
-    "/root/reference/ios_kernels/kernels/unsloth__Llama-3.2-1B-Instruct/kernel_metal_f16_20261024-1620/convert_weights.py"
-)
+# the reference's converter, relative to the reference project's root
+REF_CONVERTER = Path("ios_kernels/kernels/unsloth__Llama-3.2-1B-Instruct/kernel_metal_f16_20261024-1620/convert_weights.py")
 REPO = "tiny/llama-b200-fixture"
 CFG = dict(
     hidden_size=128,
@@ -59,6 +62,14 @@ GEN = 6
 
 
 def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("REFERENCE_ROOT"), help="root of the reference project checkout")
+    args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("pass --reference PATH (or set REFERENCE_ROOT) to the reference project's root")
+    converter = Path(args.reference) / REF_CONVERTER
+    if not converter.exists():
+        raise SystemExit(f"{converter} not found")
     torch.manual_seed(2027)
     model = LlamaForCausalLM(LlamaConfig(**CFG)).eval()
     with torch.no_grad():
@@ -73,7 +84,7 @@ def main() -> None:
         model.save_pretrained(snap, safe_serialization=True)
         out = Path(home) / "weights.bin"
         env = dict(os.environ, HOME=home)
-        subprocess.run([sys.executable, str(REF_CONVERTER), "--repo", REPO, "--out", str(out)], check=True, env=env)
+        subprocess.run([sys.executable, str(converter), "--repo", REPO, "--out", str(out)], check=True, env=env)
         shutil.copy(out, HERE / "tiny_llama_weights.bin")
     ids = torch.tensor([PROMPT])
     with torch.no_grad():

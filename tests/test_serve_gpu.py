@@ -1,4 +1,4 @@
-"""The kernel-folder binary end to end on the GPU: `kernel_folder/llm` loads the weights file
+"""The kernel-folder binary end to end on the GPU: the kernel folder's `llm` loads the weights file
 written by the reference's converter and, over the --serve protocol, returns HF transformers'
 greedy continuation of the golden prompt (tests/golden/make_weights_file.py)."""
 
@@ -14,7 +14,8 @@ from tests._tol import assert_norm_close
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
-LLM = ROOT / "gemmagemini4hackathon2026_10_2425_b200" / "kernel_folder" / "llm"
+KERNEL_DIR = ROOT / "gemmagemini4hackathon2026_10_2425_b200" / "kernels" / "unsloth__Llama-3.2-1B-Instruct" / "kernel_b200_cuda_20261202-1200"
+LLM = KERNEL_DIR / "llm"
 GOLD = ROOT / "tests" / "golden"
 
 

@@ -122,3 +122,17 @@ def test_quantized_file_errors(tmp_path):
     W.write_weights(tmp_path / "bad.bin", wf.config, t, {"l0.wo": "q8_32"})  # no l0.wo.scales
     with pytest.raises(ValueError):
         W.read_weights(tmp_path / "bad.bin")
+
+
+@pytest.mark.parametrize("fmt", ["q8_32", "q4_32"])
+def test_quantize_torch_matches_numpy(fmt):
+    """The device-side quantizer (synthetic weights) follows the same absmax rule bit for bit."""
+    import torch
+
+    r = np.random.default_rng(5)
+    w = (r.standard_normal((64, 256)) * 0.02).astype(np.float16)
+    w[3, :32] = 0  # an all-zero block: scale 0, q 0
+    q, sc = W.quantize(w, fmt)
+    qt, st = W.quantize_torch(torch.from_numpy(w), fmt)
+    np.testing.assert_array_equal(q, qt.numpy())
+    np.testing.assert_array_equal(sc.view(np.uint16), st.numpy().view(np.uint16))

@@ -4,8 +4,11 @@ b2d_paged_decode_attn_noalloc exists for callers that cannot allocate device mem
 inside another framework's memory pool, plugins whose host forbids cudaMalloc after start-up):
 it keeps its split-K scratch in a fixed device array inside the library.  This test calls it
 twice in a row, on different ragged batches, and checks each result against
-b2d_paged_decode_attn with a caller-provided workspace on identical copies of the inputs.
-The file is named so that pytest collects it last; it also passes alone in a fresh process.
+b2d_paged_decode_attn with a caller-provided workspace on identical copies of the inputs.  The
+allocation-free calls run on a side stream of their own (PyTorch creates non-blocking streams,
+which do not wait for the legacy default stream), and after each one the error query reports
+that no device-side wait gave up.  The file is named so that pytest collects it last; it also
+passes alone in a fresh process.
 """
 
 import ctypes
@@ -41,7 +44,7 @@ def _case(lens, hq, hk, hd, seed):
     return dict(kp=kp, vp=vp, qkv=qkv, table=table, lens=np.array(lens, np.int32), max_ctx=max_ctx)
 
 
-def _call(c, hq, hk, hd, theta, noalloc: bool):
+def _call(c, hq, hk, hd, theta, noalloc: bool, stream=None):
     """One call through the C ABI on fresh device copies; returns (out, k_pages, v_pages)."""
     lib = _lib.lib()
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
@@ -49,7 +52,8 @@ def _call(c, hq, hk, hd, theta, noalloc: bool):
     invf = d(O.inv_freq(hd, theta))
     B = qkv.shape[0]
     out = torch.full((B, hq * hd), float("nan"), dtype=torch.float32, device=DEV)
-    stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()  # inputs copied before a call on another stream reads them
+    stream = (stream or torch.cuda.current_stream()).cuda_stream
     common = (
         qkv.data_ptr(), _lib.F32, qkv.shape[1], kp.data_ptr(), vp.data_ptr(), table.data_ptr(),
         table.shape[1], kp.shape[0], lens.data_ptr(), invf.data_ptr(), hq, hk, hd, B,
@@ -57,6 +61,8 @@ def _call(c, hq, hk, hd, theta, noalloc: bool):
     )
     if noalloc:
         st = lib.b2d_paged_decode_attn_noalloc(*common, stream)
+        assert st == _lib.OK, lib.b2d_status_string(st)
+        st = lib.b2d_paged_decode_attn_noalloc_error()
     else:
         nbytes = lib.b2d_paged_attn_workspace_bytes(B, hq, hk, hd, c["max_ctx"])
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
@@ -72,8 +78,9 @@ def test_noalloc_matches_workspace_entry_twice():
         _case([1500, 17, 4095, 300, 0], hq, hk, hd, seed=1),  # several split-K chunks
         _case([40, 2000, 999], hq, hk, hd, seed=2),  # a second, different call
     ]
+    side = torch.cuda.Stream()
     for c in cases:
-        a, ka, va = _call(c, hq, hk, hd, theta, noalloc=True)
+        a, ka, va = _call(c, hq, hk, hd, theta, noalloc=True, stream=side)
         b, kb, vb = _call(c, hq, hk, hd, theta, noalloc=False)
         assert np.all(np.isfinite(a))
         assert_rel_close(a, b, 2e-3, what="noalloc vs workspace entry point")
