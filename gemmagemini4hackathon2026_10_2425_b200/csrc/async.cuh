@@ -95,6 +95,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Prefetch of [src, src + bytes) into L2 (no shared memory, no completion to wait for): the
+// next kernel's weights, pulled from HBM while this kernel's own stream winds down.  src 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
+}
+
+// This CTA's share of an L2 prefetch of [base, base + bytes): the range is cut into 16-byte
+// aligned slices, one per CTA of the grid, issued in pieces of at most 64 KB.
+__device__ __forceinline__ void l2_prefetch_share(const void* base, size_t bytes) {
+  if (!base || bytes < 16) return;
+  const size_t ctas = (size_t)gridDim.x * gridDim.y * gridDim.z;
+  const size_t cta = ((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  const size_t per = ((bytes / ctas) + 15) & ~size_t(15);
+  const size_t lo = cta * per, hi = lo + per < bytes ? lo + per : bytes;
+  const char* b = static_cast<const char*>(base);
+  for (size_t o = lo; o + 16 <= hi; o += 65536) {
+    const size_t n = (hi - o < 65536 ? hi - o : 65536) & ~size_t(15);
+    if (n) l2_prefetch_bulk(b + o, (uint32_t)n);
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

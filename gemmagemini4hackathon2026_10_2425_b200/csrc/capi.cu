@@ -48,9 +48,11 @@ int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, 
                       uint16_t*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
-            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
+            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t,
+            const void*, size_t);
 int tc_gemm_q(int, int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
-              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int);
+              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int,
+              const void*, size_t);
 int tc_gemm_packed(const uint8_t*, const uint8_t*, const uint16_t*, int, int, int, void*, int,
                    const float*, int, int, int, float*, int*, float*, int, void*, size_t,
                    cudaStream_t);
@@ -64,7 +66,7 @@ int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, u
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
-                      void*, size_t, cudaStream_t);
+                      void*, size_t, cudaStream_t, const void*, size_t);
 
 }  // namespace b2d
 
@@ -202,7 +204,7 @@ int b2d_gemm_tc(const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int 
                 float* logits, int* tokens, float* max_vals, int index_offset, void* workspace,
                 size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm(B2D_F16, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits,
-                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream));
+                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream), nullptr, 0);
 }
 
 int b2d_gemm_tc_ex(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
@@ -211,7 +213,7 @@ int b2d_gemm_tc_ex(int x_dtype, const uint16_t* W, const uint16_t* W_up, const u
                    int index_offset, void* workspace, size_t workspace_bytes,
                    b2d_stream_t stream) {
   return tc_gemm(x_dtype, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K, batch, logits,
-                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream));
+                 tokens, max_vals, index_offset, workspace, workspace_bytes, S(stream), nullptr, 0);
 }
 
 size_t b2d_tc_packed_bytes(int M, int K) { return tc_packed_bytes(M, K); }
@@ -234,7 +236,7 @@ int b2d_gemm_tc_q(int w_dtype, const void* q, const uint16_t* scales, const uint
                   int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
                   int batch, void* workspace, size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm_q(B2D_F16, w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
-                   batch, workspace, workspace_bytes, S(stream), nullptr, 0);
+                   batch, workspace, workspace_bytes, S(stream), nullptr, 0, nullptr, 0);
 }
 
 int b2d_gemm_tc_q_ex(int x_dtype, int w_dtype, const void* q, const uint16_t* scales,
@@ -242,7 +244,7 @@ int b2d_gemm_tc_q_ex(int x_dtype, int w_dtype, const void* q, const uint16_t* sc
                      const float* aux, int M, int K, int batch, void* workspace,
                      size_t workspace_bytes, b2d_stream_t stream) {
   return tc_gemm_q(x_dtype, w_dtype, q, scales, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
-                   batch, workspace, workspace_bytes, S(stream), nullptr, 0);
+                   batch, workspace, workspace_bytes, S(stream), nullptr, 0, nullptr, 0);
 }
 
 int b2d_tp_allreduce_add_rmsnorm(const float* const* parts, uint32_t* const* sigs,
@@ -295,7 +297,7 @@ int b2d_paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages
   return paged_decode_attn(qkv, qkv_dtype, ldqkv, k_pages, v_pages, block_table, max_blocks,
                            n_blocks, ctx_lens, inv_freq, n_heads, n_kv_heads, head_dim, batch,
                            max_ctx, scale, window, append, out, out_dtype, ldout, workspace,
-                           workspace_bytes, S(stream));
+                           workspace_bytes, S(stream), nullptr, 0);
 }
 
 }  // extern "C"

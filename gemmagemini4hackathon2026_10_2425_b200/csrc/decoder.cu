@@ -43,7 +43,7 @@ size_t paged_attn_workspace_bytes(int, int, int, int, int);
 size_t attn_ws_header_bytes(int batch, int n_kv_heads);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
-                      void*, size_t, cudaStream_t);
+                      void*, size_t, cudaStream_t, const void* pf, size_t pf_bytes);
 int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                    const float*, int, int, int, int, cudaStream_t);
 int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
@@ -52,11 +52,13 @@ int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, 
                       uint16_t*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
-            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t);
+            const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t,
+            const void* pf, size_t pf_bytes);
 int tc_gemm_multi_store(int, const uint16_t*, const uint16_t*, int, float* const*, int, int, int,
-                        int, int, void*, size_t, cudaStream_t);
+                        int, int, void*, size_t, cudaStream_t, const void* pf, size_t pf_bytes);
 int tc_gemm_q(int, int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
-              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int);
+              const float*, int, int, int, void*, size_t, cudaStream_t, float* const*, int,
+              const void* pf, size_t pf_bytes);
 int tp_allreduce_add_rmsnorm(const float* const*, uint32_t* const*, uint32_t*, int, int, int,
                              float*, const float*, float, uint16_t*, uint16_t*, int, int,
                              long long, int*, cudaStream_t);
@@ -158,6 +160,30 @@ struct b2d_decoder {
 
 static int nccl_status(ncclResult_t r) { return r == ncclSuccess ? B2D_OK : B2D_ERR_NCCL; }
 
+// Cross-kernel weight prefetch: each projection (and the attention) pulls the leading bytes of
+// the next weight-bearing kernel's matrices into L2 at its tail, so HBM keeps streaming through
+// the epilogue / launch gap between two kernels.  B2D_L2_PREFETCH_MB caps the bytes per kernel
+// (default 16 MB; 0 turns it off), read once.
+struct Pf {
+  const void* p = nullptr;
+  size_t n = 0;
+};
+
+static size_t prefetch_cap() {
+  static const size_t cap = [] {
+    const char* e = std::getenv("B2D_L2_PREFETCH_MB");
+    const long v = e ? std::atol(e) : 16;
+    return (size_t)(v > 0 ? v : 0) << 20;
+  }();
+  return cap;
+}
+
+// The first min(cap, size) bytes of a [rows, K] matrix stored as wdt (fp16 or 32-block integers).
+static Pf pf_mat(const void* W, size_t rows, size_t K, int wdt) {
+  const size_t bytes = wdt == B2D_F16 ? rows * K * 2 : (wdt == B2D_Q8_32 ? rows * K : rows * K / 2);
+  return Pf{W, std::min(bytes, prefetch_cap()) & ~size_t(15)};
+}
+
 static int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return B2D_OK;
   set_cuda_error(e);
@@ -170,7 +196,7 @@ static size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 // epilogue stores the partial straight into every rank's receive slot for this rank (the data
 // crosses NVLink while the GEMM finishes), else into the local slot for NCCL.
 static int tp_partial(b2d_decoder* h, int buf, int wdt, const uint16_t* W, const uint16_t* scales,
-                      const uint16_t* X, int K, int B, cudaStream_t s) {
+                      const uint16_t* X, int K, int B, cudaStream_t s, Pf pf) {
   const int D = h->cfg.dim;
   float* ys[kMaxTp];
   int n_ys = 0;
@@ -179,24 +205,24 @@ static int tp_partial(b2d_decoder* h, int buf, int wdt, const uint16_t* W, const
   float* mine = h->peer ? nullptr : h->recv[buf][h->rank][h->rank];
   if (wdt != B2D_F16)
     return tc_gemm_q(B2D_F16X2, wdt, W, scales, X, K, B2D_EPI_STORE, B2D_F32, mine, D, nullptr, D,
-                     K, B, h->tc_ws, h->tc_ws_bytes, s, ys, n_ys);
+                     K, B, h->tc_ws, h->tc_ws_bytes, s, ys, n_ys, pf.p, pf.n);
   if (h->peer)
     return tc_gemm_multi_store(B2D_F16X2, W, X, K, ys, n_ys, D, D, K, B, h->tc_ws,
-                               h->tc_ws_bytes, s);
+                               h->tc_ws_bytes, s, pf.p, pf.n);
   return tc_gemm(B2D_F16X2, W, nullptr, X, K, B2D_EPI_STORE, B2D_F32, mine, D, nullptr, D, K, B,
-                 nullptr, nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
+                 nullptr, nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s, pf.p, pf.n);
 }
 
 // One projection of the tensor-core step: y = epilogue(W x) with x as B2D_F16X2 planes, on the
 // fp16 or the quantized tcgen05 GEMM by the layer's weight type.
 static int tc_proj(b2d_decoder* h, int wdt, const uint16_t* W, const uint16_t* scales,
                    const uint16_t* X, int K, int epi, int y_dtype, void* y, int ldy, int M,
-                   const float* aux, int B, cudaStream_t s) {
+                   const float* aux, int B, cudaStream_t s, Pf pf) {
   if (wdt != B2D_F16)
     return tc_gemm_q(B2D_F16X2, wdt, W, scales, X, K, epi, y_dtype, y, ldy, aux, M, K, B, h->tc_ws,
-                     h->tc_ws_bytes, s, nullptr, 0);
+                     h->tc_ws_bytes, s, nullptr, 0, pf.p, pf.n);
   return tc_gemm(B2D_F16X2, W, nullptr, X, K, epi, y_dtype, y, ldy, aux, M, K, B, nullptr,
-                 nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s);
+                 nullptr, nullptr, 0, h->tc_ws, h->tc_ws_bytes, s, pf.p, pf.n);
 }
 
 // Sum the ranks' row-parallel partials (buffer `buf`) into the residual x; with gamma, also
@@ -239,7 +265,7 @@ static int tp_argmax(b2d_decoder* h, int B, int* next_tokens, cudaStream_t s) {
 // attention then only reads the pages.
 static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
                            const int* block_table, int B, bool prefill, void* out, int out_dtype,
-                           cudaStream_t s) {
+                           cudaStream_t s, Pf pf = Pf{}) {
   const b2d_model_config& c = h->cfg;
   const int HD = c.head_dim;
   if (prefill)
@@ -248,7 +274,7 @@ static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
   return paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
                            c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
                            c.max_ctx, 0.f, 0, prefill ? 0 : 1, out, out_dtype, h->hq * HD,
-                           h->attn_ws, h->attn_ws_bytes, s);
+                           h->attn_ws, h->attn_ws_bytes, s, pf.p, pf.n);
 }
 
 // Tensor-core step (batch >= kTcMinBatch): every projection's activation operand enters as
@@ -270,38 +296,47 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = h->layers[l];
     const float* next_norm = l + 1 < c.n_layers ? h->layers[l + 1].attn_norm : h->final_norm;
+    const int wd = L.wdt;
+    // what each kernel prefetches into L2: the next weight-bearing kernel's matrices
+    const Pf pf_o = pf_mat(L.wo, D, HQD, wd);
+    const Pf pf_gate = pf_mat(wd == B2D_F16 ? L.wgate : L.wup, h->fl, D, wd);
+    const Pf pf_up = pf_mat(wd == B2D_F16 ? L.wup : L.wgate, h->fl, D, wd);
+    const Pf pf_down = pf_mat(L.wdown, D, h->fl, wd);
+    const Pf pf_next = l + 1 < c.n_layers
+                           ? pf_mat(h->layers[l + 1].wqkv, h->qkv_l, D, h->layers[l + 1].wdt)
+                           : (next_tokens ? pf_mat(h->lm_head, h->lm_rows, D, B2D_F16) : Pf{});
     // QKV (column-parallel)
-    B2D_TRY(tc_proj(h, L.wdt, L.wqkv, L.sqkv, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
-                    h->qkv_l, nullptr, B, s));
+    B2D_TRY(tc_proj(h, wd, L.wqkv, L.sqkv, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
+                    h->qkv_l, nullptr, B, s, pf_o));
     // RoPE + KV append + split-K attention -> hi/lo operand of the O projection
-    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s));
+    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s, pf_gate));
     // O projection (row-parallel) + residual, then RMSNorm(ffn) -> hi/lo
     if (!tpar) {
-      B2D_TRY(tc_proj(h, L.wdt, L.wo, L.so, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, D,
-                      nullptr, B, s));
+      B2D_TRY(tc_proj(h, wd, L.wo, L.so, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, D,
+                      nullptr, B, s, pf_up));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, xn_lo, B, D, s));
     } else {
-      B2D_TRY(tp_partial(h, 0, L.wdt, L.wo, L.so, h->att16, HQD, B, s));
+      B2D_TRY(tp_partial(h, 0, wd, L.wo, L.so, h->att16, HQD, B, s, pf_up));
       B2D_TRY(tp_reduce(h, 0, L.ffn_norm, h->xn16, B, h->peer, s));
     }
     // gate/up SwiGLU (column-parallel) -> hi/lo.  fp16 weights: one dual-matrix GEMM; quantized
     // weights: the up projection into hid (fp32), then the gate projection times it.
-    if (L.wdt == B2D_F16) {
+    if (wd == B2D_F16) {
       B2D_TRY(tc_gemm(X2, L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, X2, h->h16, h->fl, nullptr,
-                      h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s));
+                      h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s, pf_down.p, pf_down.n));
     } else {
-      B2D_TRY(tc_proj(h, L.wdt, L.wup, L.sup, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->hid, h->fl,
-                      h->fl, nullptr, B, s));
-      B2D_TRY(tc_proj(h, L.wdt, L.wgate, L.sgate, h->xn16, D, B2D_EPI_SILU_MUL, X2, h->h16, h->fl,
-                      h->fl, h->hid, B, s));
+      B2D_TRY(tc_proj(h, wd, L.wup, L.sup, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->hid, h->fl,
+                      h->fl, nullptr, B, s, Pf{}));
+      B2D_TRY(tc_proj(h, wd, L.wgate, L.sgate, h->xn16, D, B2D_EPI_SILU_MUL, X2, h->h16, h->fl,
+                      h->fl, h->hid, B, s, pf_down));
     }
     // down (row-parallel) + residual, then the next RMSNorm -> hi/lo
     if (!tpar) {
-      B2D_TRY(tc_proj(h, L.wdt, L.wdown, L.sdown, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, D,
-                      nullptr, B, s));
+      B2D_TRY(tc_proj(h, wd, L.wdown, L.sdown, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, D,
+                      nullptr, B, s, pf_next));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, xn_lo, B, D, s));
     } else {
-      B2D_TRY(tp_partial(h, 1, L.wdt, L.wdown, L.sdown, h->h16, h->fl, B, s));
+      B2D_TRY(tp_partial(h, 1, wd, L.wdown, L.sdown, h->h16, h->fl, B, s, pf_next));
       B2D_TRY(tp_reduce(h, 1, next_norm, h->xn16, B, h->peer, s));
     }
   }
@@ -310,11 +345,12 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   const int offset = h->rank * h->lm_stride;
   if (!tpar) {
     B2D_TRY(tc_gemm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
-                    nullptr, h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s));
+                    nullptr, h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s,
+                    nullptr, 0));
   } else {
     B2D_TRY(tc_gemm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
                     nullptr, h->lm_rows, D, B, logits, h->am_idx[h->rank], h->am_val[h->rank],
-                    offset, ws, wsb, s));
+                    offset, ws, wsb, s, nullptr, 0));
     B2D_TRY(tp_argmax(h, B, next_tokens, s));
   }
   return B2D_OK;

@@ -34,6 +34,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "async.cuh"
@@ -80,7 +81,17 @@ struct Params {
   // partial sums pushed straight into every rank's receive buffer over NVLink
   float* ys[8];
   int n_ys;
+  // the next kernel's weights, pulled into L2 by this kernel's tail (nullptr: none)
+  const void* pf;
+  unsigned long long pf_bytes;
+  // accumulation chains per CTA (1..kMaxChains): k-tile i accumulates into TMEM accumulator
+  // i % chains, and the epilogue adds the chains in fp32 in a fixed order.  Tensor-core
+  // accumulation over a long run of MMAs is measurably less exact than round-to-nearest fp32
+  // adds; short chains keep each run to a few k-tiles.
+  int chains;
+  uint32_t tmem_cols;  // TMEM columns the CTA allocates (power of two >= 32)
 };
+constexpr int kMaxChains = 4;
 
 // y[yi] = v into y, or into every copy in p.ys
 template <typename P>
@@ -243,8 +254,7 @@ struct Cfg {
   // 16-byte reads of consecutive rows fall in distinct banks); ks x (BM / ks) = BM rows in all
   static constexpr int RED_FLOATS = NACC * BM * (N + 4);
   static constexpr int SMEM = RING_BYTES + RED_FLOATS * 4 + 1024;  // + alignment slack
-  static constexpr int ACC_COLS = NB * NACC;  // TMEM columns the accumulators use
-  static constexpr uint32_t TMEM_COLS = ACC_COLS <= 32 ? 32 : (ACC_COLS <= 64 ? 64 : 128);
+  static constexpr int ACC_COLS = NB * NACC;  // TMEM columns of one accumulation chain
   // CTAs of this kernel one SM holds (228 KB of shared memory per SM, ~1 KB reserved per CTA,
   // plus the kernel's static shared memory)
   static constexpr int CTAS_PER_SM = 2 * (SMEM + 4096) <= 228 * 1024 ? 2 : 1;
@@ -319,9 +329,10 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&tmem_slot)),
-                 "r"(C::TMEM_COLS));
+                 "r"(p.tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  const int chains = min(p.chains, max(nkt, 1));  // chains this CTA writes (each at least once)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -381,10 +392,14 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
           tma_load_2d(st + C::B_OFF + N * BK * 2, &p.tmB2, (kt_begin + i) * BK, 0, &full_bar[s]);
       }
     }
+    // this CTA's weights are all requested: start pulling the next kernel's into L2, so HBM
+    // stays busy through this kernel's epilogue and the next one's launch
+    if (!abort_flag) l2_prefetch_share(p.pf, p.pf_bytes);
   } else if (warp == 1 && lane == 0) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = idesc_f16<C::NB>();
     bool ok = true;
+    int chain = 0;
     for (int i = 0; i < nkt; ++i) {
       const int s = QUANT ? i % C::AS : i % C::STAGES;
       const int ph = QUANT ? (i / C::AS) & 1 : (i / C::STAGES) & 1;
@@ -397,15 +412,17 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       uint8_t* st = smem + s * C::STAGE_BYTES;
       const uint64_t a = smem_desc_sw128(st);
       const uint64_t b = smem_desc_sw128(st + C::B_OFF);
+      const uint32_t dacc = tmem + (uint32_t)(chain * C::ACC_COLS);  // this k-tile's chain
 #pragma unroll
       for (int k = 0; k < BK / 16; ++k) {  // 32 bytes of K per MMA: +2 in the 16-byte address field
-        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-        mma_f16(tmem, a + 2 * k, b + 2 * k, idesc, acc);
+        const uint32_t acc = (i >= chains || k > 0) ? 1u : 0u;
+        mma_f16(dacc, a + 2 * k, b + 2 * k, idesc, acc);
         if (DUAL) {
           const uint64_t a2 = smem_desc_sw128(st + C::A_BYTES);
-          mma_f16(tmem + C::NB, a2 + 2 * k, b + 2 * k, idesc, acc);
+          mma_f16(dacc + C::NB, a2 + 2 * k, b + 2 * k, idesc, acc);
         }
       }
+      chain = chain + 1 == chains ? 0 : chain + 1;
       mma_commit(QUANT ? &a_empty[s] : &empty_bar[s]);  // slot free once these MMAs read it
     }
     if (ok) mma_commit(&done_bar);
@@ -422,11 +439,39 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
       const uint32_t s1 = 2 * kt + 1 < nsb ? (uint32_t)__ldg(srow + 2 * kt + 1) : 0u;
       return s0 | (s1 << 16);
     };
-    uint32_t sc_next = scale_pair(kt_begin);
+    // The row's scales come from HBM: fetching them one k-tile ahead put a memory latency on
+    // every k-tile.  When the rows hold whole 16-byte groups (K % 256 == 0), each 16-byte load
+    // brings 4 k-tiles' scales and a ring of three such loads runs 8-12 k-tiles ahead.
+    const bool vec_sc = (p.K % 256) == 0 && (reinterpret_cast<uintptr_t>(p.scales) & 15) == 0;
+    auto scale_group = [&](int g) -> uint4 {  // scales of k-tiles 4g .. 4g + 3
+      if (grow >= p.M || 4 * g >= p.k_tiles) return make_uint4(0u, 0u, 0u, 0u);
+      return __ldg(reinterpret_cast<const uint4*>(srow) + g);
+    };
+    int g0 = kt_begin >> 2;
+    uint4 sg0 = make_uint4(0u, 0u, 0u, 0u), sg1 = sg0, sg2 = sg0;
+    if (vec_sc) {
+      sg0 = scale_group(g0);
+      sg1 = scale_group(g0 + 1);
+      sg2 = scale_group(g0 + 2);
+    }
+    uint32_t sc_next = vec_sc ? 0u : scale_pair(kt_begin);
     for (int i = 0; i < nkt; ++i) {
       const int rs = i % C::RS, as = i % C::AS;
-      const uint32_t sc = sc_next;
-      if (i + 1 < nkt) sc_next = scale_pair(kt_begin + i + 1);
+      uint32_t sc;
+      if (vec_sc) {
+        const int kt = kt_begin + i;
+        if ((kt >> 2) > g0) {  // next group: rotate the ring and fetch three groups ahead
+          sg0 = sg1;
+          sg1 = sg2;
+          sg2 = scale_group(g0 + 3);
+          ++g0;
+        }
+        const int w = kt & 3;
+        sc = w == 0 ? sg0.x : (w == 1 ? sg0.y : (w == 2 ? sg0.z : sg0.w));
+      } else {
+        sc = sc_next;
+        if (i + 1 < nkt) sc_next = scale_pair(kt_begin + i + 1);
+      }
       if (!mbar_wait(&raw_full[rs], (i / C::RS) & 1, p.err, ERR_TIMEOUT_FULL) ||
           (i >= C::AS &&
            !mbar_wait(&a_empty[as], ((i / C::AS) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))) {
@@ -516,18 +561,24 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   float acc[N], acc2[DUAL ? N : 1];
   const bool epi_warp = warp >= EPI0 && warp < EPI0 + 4;
   if (have && epi_warp) {
+    // sum of the chains (and of the hi / lo plane columns of each token), in a fixed order
     const uint32_t taddr = tmem + (uint32_t((warp & 3) * 32) << 16);
     tmem_ld<N>(taddr, acc);
     if (DUAL) tmem_ld<N>(taddr + C::NB, acc2);
-    if constexpr (XS == 2) {  // add the lo-plane columns of each token
-      float lo[N];
-      tmem_ld<N>(taddr + N, lo);
+    float part[N];
+    for (int ch = 0; ch < chains; ++ch) {
+      const uint32_t ca = taddr + (uint32_t)(ch * C::ACC_COLS);
 #pragma unroll
-      for (int t = 0; t < N; ++t) acc[t] += lo[t];
-      if constexpr (DUAL) {
-        tmem_ld<N>(taddr + C::NB + N, lo);
+      for (int pl = 0; pl < XS; ++pl) {
+        if (ch == 0 && pl == 0) continue;  // loaded above
+        tmem_ld<N>(ca + pl * N, part);
 #pragma unroll
-        for (int t = 0; t < N; ++t) acc2[t] += lo[t];
+        for (int t = 0; t < N; ++t) acc[t] += part[t];
+        if constexpr (DUAL) {
+          tmem_ld<N>(ca + C::NB + pl * N, part);
+#pragma unroll
+          for (int t = 0; t < N; ++t) acc2[t] += part[t];
+        }
       }
     }
   }
@@ -535,7 +586,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   __syncthreads();
   if (warp == 0) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(C::TMEM_COLS));
+                 "r"(p.tmem_cols));
   }
   const bool ok = have && !abort_flag;  // CTA-uniform
   const int r = (warp & 3) * 32 + lane;       // row within the tile (epilogue warps)
@@ -866,6 +917,54 @@ struct TcCall {
   int xs = 1;     // activation planes: 1 fp16, 2 hi + lo fp16
 };
 
+// Accumulation chains and the TMEM allocation for a call: one chain per 8 k-tiles of a CTA's
+// K range (at most kMaxChains), within the TMEM its co-resident CTAs leave (512 columns per SM).
+// B2D_TC_CHAIN_KTILES overrides the 8 (a tuning knob, read once).
+static void pick_chains(tc::Params& p, int acc_cols, int ctas_per_sm) {
+  static const int ktiles_per_chain = [] {
+    const char* e = std::getenv("B2D_TC_CHAIN_KTILES");
+    const int v = e ? std::atoi(e) : 8;
+    return v > 0 ? v : 8;
+  }();
+  const int nkt = (p.k_tiles + p.k_splits - 1) / p.k_splits;
+  int c = std::min(tc::kMaxChains, std::max(1, (nkt + ktiles_per_chain - 1) / ktiles_per_chain));
+  auto cols = [&](int ch) {
+    uint32_t n = 32;
+    while (n < (uint32_t)(ch * acc_cols)) n <<= 1;
+    return n;
+  };
+  while (c > 1 && cols(c) * ctas_per_sm > 512) --c;
+  p.chains = c;
+  p.tmem_cols = cols(c);
+}
+
+template <int N, bool DUAL, int QUANT, int XS>
+static void pick_chains_t(tc::Params& p) {
+  using C = tc::Cfg<N, DUAL, QUANT, XS>;
+  pick_chains(p, C::ACC_COLS, C::CTAS_PER_SM);
+}
+
+static void pick_chains_for(tc::Params& p, int n_tile, bool dual, int quant, int xs) {
+#define B2D_CH(NT, DU, QU, X)                                 \
+  if (n_tile == NT && dual == DU && quant == QU && xs == X) { \
+    pick_chains_t<NT, DU, QU, X>(p);                          \
+    return;                                                   \
+  }
+#define B2D_CH_Q(NT, DU, X) B2D_CH(NT, DU, 0, X) B2D_CH(NT, DU, 1, X) B2D_CH(NT, DU, 2, X)
+  B2D_CH_Q(16, false, 1)
+  B2D_CH_Q(16, false, 2)
+  B2D_CH_Q(32, false, 1)
+  B2D_CH_Q(32, false, 2)
+  B2D_CH(16, true, 0, 1)
+  B2D_CH(16, true, 0, 2)
+  B2D_CH(32, true, 0, 1)
+  B2D_CH(32, true, 0, 2)
+#undef B2D_CH_Q
+#undef B2D_CH
+  p.chains = 1;
+  p.tmem_cols = 128;
+}
+
 // Split count for a call's kernel variant.
 static int pick_splits(int n_tile, bool dual, int quant, int xs, int m_tiles, int k_tiles) {
 #define B2D_PICK(NT, DU, QU, X)                          \
@@ -949,6 +1048,7 @@ int tc_gemm_prepare(TcCall* call, int x_dtype, const uint16_t* W, const uint16_t
   }
   if (epilogue != B2D_EPI_ARGMAX)
     p.k_splits = pick_splits(pl.n_tile, epilogue == B2D_EPI_SWIGLU, 0, xs, pl.m_tiles, pl.k_tiles);
+  pick_chains_for(p, pl.n_tile, epilogue == B2D_EPI_SWIGLU, 0, xs);
   call->grid = dim3(pl.m_tiles, p.k_splits);
   call->n_tile = pl.n_tile;
   call->dual = epilogue == B2D_EPI_SWIGLU;
@@ -983,11 +1083,14 @@ int tc_gemm_launch(const TcCall& c, cudaStream_t stream) {
 int tc_gemm(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t* X, int ldx,
             int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M, int K,
             int batch, float* logits, int* tokens, float* max_vals, int index_offset,
-            void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+            void* workspace, size_t workspace_bytes, cudaStream_t stream,
+            const void* pf = nullptr, size_t pf_bytes = 0) {
   TcCall c;
   B2D_TRY(tc_gemm_prepare(&c, x_dtype, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
                           batch, logits, tokens, max_vals, index_offset, workspace,
                           workspace_bytes));
+  c.prm.pf = pf;
+  c.prm.pf_bytes = pf_bytes;
   return tc_gemm_launch(c, stream);
 }
 
@@ -995,11 +1098,14 @@ int tc_gemm(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t
 // rank's receive buffer.
 int tc_gemm_multi_store(int x_dtype, const uint16_t* W, const uint16_t* X, int ldx,
                         float* const* ys, int n_ys, int ldy, int M, int K, int batch,
-                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                        const void* pf = nullptr, size_t pf_bytes = 0) {
   TcCall c;
   B2D_TRY(tc_gemm_prepare(&c, x_dtype, W, nullptr, X, ldx, B2D_EPI_STORE, B2D_F32, nullptr, ldy,
                           nullptr, M, K, batch, nullptr, nullptr, nullptr, 0, workspace,
                           workspace_bytes, false, ys, n_ys));
+  c.prm.pf = pf;
+  c.prm.pf_bytes = pf_bytes;
   return tc_gemm_launch(c, stream);
 }
 
@@ -1060,7 +1166,7 @@ int tc_pack_f16(const uint16_t* W, int ldw, int M, int K, void* out, cudaStream_
 int tc_gemm_q(int x_dtype, int w_dtype, const void* q, const uint16_t* scales, const uint16_t* X,
               int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
               int K, int batch, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-              float* const* ys, int n_ys) {
+              float* const* ys, int n_ys, const void* pf = nullptr, size_t pf_bytes = 0) {
   if (!q || !scales || !X || (!y && n_ys == 0)) return B2D_ERR_NULL;
   if (w_dtype != B2D_Q8_32 && w_dtype != B2D_Q4_32) return B2D_ERR_UNSUPPORTED;
   if (x_dtype != B2D_F16 && x_dtype != B2D_F16X2) return B2D_ERR_UNSUPPORTED;
@@ -1108,7 +1214,10 @@ int tc_gemm_q(int x_dtype, int w_dtype, const void* q, const uint16_t* scales, c
     if (!ys[i]) return B2D_ERR_NULL;
     p.ys[i] = ys[i];
   }
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
   p.k_splits = pick_splits(pl.n_tile, false, quant, xs, pl.m_tiles, pl.k_tiles);
+  pick_chains_for(p, pl.n_tile, false, quant, xs);
   c.grid = dim3(pl.m_tiles, p.k_splits);
   c.n_tile = pl.n_tile;
   c.dual = false;

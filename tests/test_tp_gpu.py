@@ -3,7 +3,10 @@
 Each world size runs only where that many GPUs are visible; each rank is a spawned process that builds its
 DecodeEngine shard, runs one step (CUDA-core path at batch 5, tensor-core path at batch 24),
 with the peer-memory collectives and with NCCL (B2D_TP_COLLECTIVE=nccl),
-and sends its vocab-shard logits and the combined next tokens back to the test.
+and sends its vocab-shard logits and the combined next tokens back to the test.  A q8_32 case
+shards quantized projections (rows of the column-parallel ones, 32-element K blocks of the
+row-parallel ones) and checks them against the oracle fed the weights the tcgen05 path
+multiplies, fp16(scale * q).
 """
 
 import os
@@ -41,7 +44,21 @@ def _case(batch):
     return cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens
 
 
-def _rank(rank, world, port, batch, collective, q):
+def _quantized(w, cfg, fmt):
+    """(stored tensors, quant map, fp16(scale * q) weights) with every projection quantized."""
+    from gemmagemini4hackathon2026_10_2425_b200 import weights as W
+
+    stored, quant, rounded = dict(w), {}, dict(w)
+    for i in range(cfg.n_layers):
+        for n in ("wqkv", "wo", "wgate", "wup", "wdown"):
+            name = f"l{i}.{n}"
+            qv, sc = W.quantize(w[name], fmt)
+            stored[name], stored[name + ".scales"], quant[name] = qv, sc, fmt
+            rounded[name] = W.dequantize(qv, sc, fmt).astype(np.float16)
+    return stored, quant, rounded
+
+
+def _rank(rank, world, port, batch, collective, q, fmt=None):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -61,7 +78,11 @@ def _rank(rank, world, port, batch, collective, q):
         for i in range(cfg.n_layers):  # this rank's KV heads
             eng.k_pages[i].copy_(torch.from_numpy(np.ascontiguousarray(kp[i][:, rank * hk : (rank + 1) * hk])))
             eng.v_pages[i].copy_(torch.from_numpy(np.ascontiguousarray(vp[i][:, rank * hk : (rank + 1) * hk])))
-        eng.load_weights({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()})
+        if fmt:
+            stored, quant, _ = _quantized(w, cfg, fmt)
+            eng.load_weights({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in stored.items()}, quant)
+        else:
+            eng.load_weights({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in w.items()})
         i32 = lambda a: torch.tensor(np.asarray(a, np.int32), device=dev)
         tok, ln, tb = i32(tokens), i32(lens), torch.from_numpy(table).to(dev)
         nxt = torch.empty_like(tok)
@@ -81,17 +102,19 @@ def _rank(rank, world, port, batch, collective, q):
     "world",
     [pytest.param(w, marks=pytest.mark.skipif(torch.cuda.device_count() < w, reason=f"needs {w} GPUs")) for w in (2, 4, 8)],
 )
-@pytest.mark.parametrize("collective", ["peer", "nccl"])
-@pytest.mark.parametrize("batch", [5, 24])
+@pytest.mark.parametrize(
+    "collective,batch,fmt",
+    [("peer", 5, None), ("peer", 24, None), ("nccl", 5, None), ("nccl", 24, None), ("peer", 24, "q8_32")],
+)
 @pytest.mark.timeout(600)
-def test_tp_decode_step_matches_oracle(batch, collective, world):
+def test_tp_decode_step_matches_oracle(batch, collective, fmt, world):
     from oracle import step as S
     from tests._tol import assert_norm_close
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, batch, collective, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, batch, collective, q, fmt)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
@@ -103,6 +126,8 @@ def test_tp_decode_step_matches_oracle(batch, collective, world):
         p.join(timeout=120)
         assert p.exitcode == 0
     cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens = _case(batch)
+    if fmt:
+        w = _quantized(w, cfg, fmt)[2]
     ref_logits, ref_next = S.decode_step(w, cfg, tokens, lens, table, kp, vp)
     logits = np.concatenate([got[r][0] for r in range(world)], axis=1)
     assert_norm_close(logits, ref_logits, 2e-3, what=f"tp{world} logits b{batch}")
