@@ -52,8 +52,8 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -63,14 +63,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Per-slot barrier among the tp ranks.  Thread r < tp announces this rank to rank r and then
-// waits for rank r's announcement.  The data a rank announces was written by the previous kernel
-// on that rank (its partial in its own memory, or pushed into the peers' receive slots); that
-// grid completed before this kernel passed griddepcontrol.wait, so those writes precede the
-// announcement in causality order.  The announcement is a release store at system scope and the
-// poll an acquire load at system scope: a peer that observes the epoch therefore observes the
-// data too (PTX memory model, release/acquire pattern across GPUs), and the CTA barrier that
-// follows carries that to every thread of the reader's CTA, whose loads bypass L1.  Only the
-// flag word is released / acquired (one thread per peer), not a full system-scope fence.
+// waits for rank r's announcement.
+//  * Writer: the data a rank announces was written by the previous kernel on that rank (its
+//    partial in its own memory, or pushed into the peers' receive slots over NVLink).  This
+//    kernel stores the flag only after griddepcontrol.wait, which returns once that grid has
+//    completed and its memory operations are performed -- the pushed partials have reached the
+//    peers' memory before the flag store is even issued.  The flag is therefore a relaxed
+//    system-scope store: a release store (or fence) at system scope would add a full
+//    system-scope memory barrier per flag, which measured 15.6 instead of ~5 us per all-reduce
+//    kernel at TP8 on B200s (per-kernel timeline of the graph-replayed step).
+//  * Reader: polls with acquire loads at system scope, so nothing after the poll (the sums below,
+//    L1-bypassing loads) is performed before the flag value is observed; the CTA barrier that
+//    follows carries that order to every thread of the CTA.
 // Returns false (CTA-uniform) if some peer did not arrive within timeout_ns; *err then holds
 // B2D_ERR_TIMEOUT.
 __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, uint32_t* epochs,
@@ -86,7 +90,7 @@ __device__ bool peer_barrier(uint32_t* const* sig, int rank, int tp, int slot, u
   bool ok = true;
   if (threadIdx.x < tp) {
     const int r = threadIdx.x;
-    st_release_sys(sig[r] + slot * kSigStride + rank, e);
+    st_relaxed_sys(sig[r] + slot * kSigStride + rank, e);
     const uint32_t* mine = sig[rank] + slot * kSigStride + r;
     if ((int)(ld_acquire_sys(mine) - e) < 0) {
       const uint64_t t0 = global_ns();

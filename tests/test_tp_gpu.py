@@ -10,7 +10,6 @@ multiplies, fp16(scale * q).
 """
 
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -20,10 +19,14 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous() -> str:
+    """A file rendezvous for the spawned ranks (no TCP port to race for between tests)."""
+    import tempfile
+
+    fd, path = tempfile.mkstemp(prefix="b2d_tp_rdzv_")
+    os.close(fd)
+    os.unlink(path)  # the store creates it
+    return "file://" + path
 
 
 def _case(batch):
@@ -58,17 +61,17 @@ def _quantized(w, cfg, fmt):
     return stored, quant, rounded
 
 
-def _rank(rank, world, port, batch, collective, q, fmt=None):
+def _rank(rank, world, rdzv, batch, collective, q, fmt=None):
     import torch.distributed as dist
     from datetime import timedelta
 
     from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, share_nccl_id
     from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), B2D_TP_COLLECTIVE=collective)
+    os.environ.update(B2D_TP_COLLECTIVE=collective)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
     try:
         cfg, w, lens, max_ctx, nblk, table, kp, vp, tokens = _case(batch)
         shape = ModelShape(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
@@ -113,8 +116,8 @@ def test_tp_decode_step_matches_oracle(batch, collective, fmt, world):
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, batch, collective, q, fmt)) for r in range(world)]
+    rdzv = _rendezvous()
+    procs = [ctx.Process(target=_rank, args=(r, world, rdzv, batch, collective, q, fmt)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
@@ -136,7 +139,7 @@ def test_tp_decode_step_matches_oracle(batch, collective, fmt, world):
     np.testing.assert_array_equal(got[0][1], np.argmax(logits, axis=1))
 
 
-def _prefill_rank(rank, world, port, q):
+def _prefill_rank(rank, world, rdzv, q):
     """One rank of a tensor-parallel prefill: 40 prompt tokens (a 32-row tensor-core chunk and an
     8-row CUDA-core chunk), then the last position's logits shard."""
     import torch.distributed as dist
@@ -145,10 +148,9 @@ def _prefill_rank(rank, world, port, q):
     from gemmagemini4hackathon2026_10_2425_b200.engine import DecodeEngine, share_nccl_id
     from gemmagemini4hackathon2026_10_2425_b200.tp import ModelShape
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+    dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
     try:
         cfg, w, ids, table_row = _prefill_case()
         shape = ModelShape(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
@@ -192,8 +194,8 @@ def test_tp_prefill_matches_oracle(world):
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_prefill_rank, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rendezvous()
+    procs = [ctx.Process(target=_prefill_rank, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
