@@ -482,6 +482,38 @@ def config5_engine(dev, steps_total: int, rank: int = 0, world: int = 1, nccl_id
     return eng, table, lens, tokens0
 
 
+def step_timeline(eng, tok, ctx, table, nxt, steps: int = 4) -> dict:
+    """Per-kernel device timeline of the graph-replayed step on this rank: CUPTI kernel records
+    (torch.profiler, no kernel replay, kernels overlap as in the timed run) of `steps` steps, the
+    last step's kernels aggregated by name, and per launch: start, duration and the gap to the
+    previous kernel's end (negative = overlap through programmatic dependent launch)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    s = eng.stream
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with torch.cuda.stream(s):
+            for _ in range(steps):
+                eng.step(tok, ctx, table, nxt)
+        torch.cuda.synchronize()
+    ks = sorted(
+        ((e.time_range.start, e.time_range.end, e.name) for e in prof.events() if e.device_type.name == "CUDA"),
+        key=lambda t: t[0],
+    )
+    per = len(ks) // steps
+    one = ks[-per:]
+    t0, prev_end = one[0][0], one[0][0]
+    agg, launches = {}, []
+    for st, en, name in one:
+        short = name.split("(")[0]
+        a = agg.setdefault(short, {"launches": 0, "total_us": 0.0})
+        a["launches"] += 1
+        a["total_us"] += en - st
+        launches.append([round(st - t0, 2), round(en - st, 2), round(st - prev_end, 2), short])
+        prev_end = max(prev_end, en)
+    return {"kernels_per_step": per, "span_us": max(k[1] for k in one) - t0, "by_kernel": agg, "launches": launches}
+
+
 def quantized_step(args, shape, lens, tokens0, dev, peak) -> dict:
     """The config-5 step (batch 32, graph replay) and tg128 with the layers' projections stored
     as q8_32 / q4_32 (1.06 / 0.56 bytes per weight streamed instead of 2), on one GPU."""
@@ -605,6 +637,18 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    if args.timeline:  # the per-kernel timeline instead of the rest of the measurements
+        tl = step_timeline(eng, tok_d, ctx_d, table, nxt_d)
+        # and one sequence alone (the batch-1 path of the reference's tg128)
+        tl1 = step_timeline(eng, tok_d[:1], ctx_d[:1], table[:1].contiguous(), nxt_d[:1])
+        if rank == 0:
+            print(json.dumps({"timeline": tl, "timeline_batch1": tl1, "n_gpus": world, "ms_per_step": ms}), flush=True)
+        eng.close()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        return
 
     # launches per step: capture-time count of a fresh graph (launch counter is per thread)
     c0 = _lib.lib().b2d_launch_counter()
@@ -809,6 +853,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op (configs 1-4) microbenchmarks")
+    ap.add_argument("--timeline", action="store_true", help="after the timed steps, print rank 0's per-kernel device timeline of the graph-replayed step (CUPTI kernel records) instead of the rest of the measurements")
     ap.add_argument("--op", help="run only the config 1-4 microbenchmark(s) whose key starts with OP (e.g. c4, c2_f16_2048to2048) for --steps iterations, print their JSON and exit")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # timing rule: at least 3 warm-up steps

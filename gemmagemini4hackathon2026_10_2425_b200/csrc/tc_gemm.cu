@@ -901,7 +901,13 @@ static int tc_pick_splits(int m_tiles, int k_tiles) {
   using C = tc::Cfg<N, DUAL, QUANT, XS>;
   const int per_sm = !DUAL && !QUANT ? std::min(B2D_TC_SPLIT_CTAS_PER_SM, C::CTAS_PER_SM) : 1;
   const int slots = per_sm * num_sms();
-  for (int ks = 8; ks >= 2; ks >>= 1)
+  // B2D_TC_MAX_SPLITS caps the split count (a tuning knob, read once; default 8)
+  static const int max_ks = [] {
+    const char* e = std::getenv("B2D_TC_MAX_SPLITS");
+    const int v = e ? std::atoi(e) : tc::kMaxSplits;
+    return v >= 1 && v <= tc::kMaxSplits ? v : tc::kMaxSplits;
+  }();
+  for (int ks = max_ks; ks >= 2; ks >>= 1)
     if (ks <= k_tiles && m_tiles * ks <= slots) return ks;
   return 1;
 }

@@ -105,3 +105,30 @@ def test_shard_layout_matches_oracle_slices():
             assert len(rows) == (cfg.n_heads + 2 * cfg.n_kv_heads) // tp * hd
     with pytest.raises(ValueError):
         T.check_tp(shape, 3)
+
+
+@pytest.mark.parametrize("fmt", ["q8_32", "q4_32"])
+@pytest.mark.parametrize("tp", [2, 8])
+def test_quantized_shards_dequantize_to_the_fp16_shards(fmt, tp):
+    """shard_layer_quant cuts the stored integers and their scales so that every rank's shard
+    dequantizes to exactly the same slice of the dequantized matrix that shard_layer gives the
+    fp16 path (rows of the column-parallel projections, 32-element K blocks of the row-parallel
+    ones), and the shards put back together are the whole matrix."""
+    from gemmagemini4hackathon2026_10_2425_b200 import weights as W
+
+    cfg = S.ModelConfig(512, 1, 16, 8, 64, 2048, 1000, 1e-5, 1e4)
+    shape = T.ModelShape(cfg.dim, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.vocab, cfg.eps, cfg.theta)
+    w = S.synth_weights(cfg, seed=3)
+    full_q, full_deq = {}, {}
+    for n in ("wqkv", "wo", "wgate", "wup", "wdown"):
+        q, sc = W.quantize(w[f"l0.{n}"], fmt)
+        full_q[n], full_q[n + ".scales"] = torch.from_numpy(q), torch.from_numpy(sc)
+        full_deq[n] = torch.from_numpy(W.dequantize(q, sc, fmt))
+    full_q["attn_norm"] = full_q["ffn_norm"] = torch.ones(cfg.dim)
+    full_deq["attn_norm"] = full_deq["ffn_norm"] = torch.ones(cfg.dim)
+    for r in range(tp):
+        qs = T.shard_layer_quant(full_q, shape, r, tp, fmt)
+        fs = T.shard_layer(full_deq, shape, r, tp)
+        for n in ("wqkv", "wo", "wgate", "wup", "wdown"):
+            deq = W.dequantize(qs[n].numpy(), qs[n + ".scales"].numpy(), fmt)
+            np.testing.assert_array_equal(deq, fs[n].numpy())
