@@ -45,7 +45,7 @@ int attn_chunk_tokens(int, int, int);
 int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
                     cudaStream_t);
 int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*,
-                      uint16_t*, int, int, cudaStream_t);
+                      uint16_t*, float*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t,
@@ -192,7 +192,7 @@ int b2d_add_rmsnorm(float* x, const float* p, const float* gamma, float eps, int
 
 int b2d_embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
                           float eps, uint16_t* out, int D, int batch, b2d_stream_t stream) {
-  return embed_rmsnorm_f16(E, tokens, x, gamma, eps, out, nullptr, D, batch, S(stream));
+  return embed_rmsnorm_f16(E, tokens, x, gamma, eps, out, nullptr, nullptr, D, batch, S(stream));
 }
 
 size_t b2d_gemm_tc_workspace_bytes(int M, int K, int batch, int epilogue) {

@@ -155,4 +155,23 @@ inline int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
   return B2D_OK;
 }
 
+// RMSNorm folded into a tensor-core GEMM pair (tc_gemm_norm): a residual-add producer emits
+// the un-normalized operand and per-slice sums of squares, its consumer scales its product by
+// the norm factor.  Producer fields (gamma set): gamma of the next norm [M], planes (hi / lo
+// fp16 of y * gamma * e[t], lo at + batch * ldy), part_out ([32][M / 16] slice sums, then
+// e[32]), r_prev (the last norm factor per token, for e[t]; nullptr: e = 1).  Consumer fields
+// (part_in set): a producer's part_out, r_out (the norm factor per token, optional), eps.
+struct TcNorm {
+  const float* gamma = nullptr;
+  uint16_t* planes = nullptr;
+  float* part_out = nullptr;
+  const float* r_prev = nullptr;
+  const float* part_in = nullptr;
+  float* r_out = nullptr;
+  float eps = 0.f;
+};
+
+// Floats of one TcNorm slice-sum block for M rows: [32][M / 16] sums, then e[32].
+inline size_t tc_norm_part_floats(int M) { return (size_t)32 * (M / 16) + 32; }
+
 }  // namespace b2d

@@ -49,11 +49,14 @@ int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, 
 int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
                     cudaStream_t);
 int embed_rmsnorm_f16(const uint16_t*, const int*, float*, const float*, float, uint16_t*,
-                      uint16_t*, int, int, cudaStream_t);
+                      uint16_t*, float*, int, int, cudaStream_t);
 size_t tc_gemm_workspace_bytes(int M, int K, int batch, int epilogue);
 int tc_gemm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
             const float*, int, int, int, float*, int*, float*, int, void*, size_t, cudaStream_t,
             const void* pf, size_t pf_bytes);
+int tc_gemm_norm(int, const uint16_t*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
+                 const float*, int, int, int, float*, int*, void*, size_t, cudaStream_t,
+                 const void* pf, size_t pf_bytes, const TcNorm& nrm);
 int tc_gemm_multi_store(int, const uint16_t*, const uint16_t*, int, float* const*, int, int, int,
                         int, int, void*, size_t, cudaStream_t, const void* pf, size_t pf_bytes);
 int tc_gemm_q(int, int, const void*, const uint16_t*, const uint16_t*, int, int, int, void*, int,
@@ -132,6 +135,10 @@ struct b2d_decoder {
   uint16_t* xn16 = nullptr;   // [2][B, D]   rmsnorm(x) * gamma
   uint16_t* att16 = nullptr;  // [2][B, hq*HD]  attention output
   uint16_t* h16 = nullptr;    // [2][B, fl]  SwiGLU output
+  // single-GPU tensor-core step with the RMSNorms folded into the GEMMs (TcNorm): two
+  // slice-sum blocks (after the O and the down projection) and the last norm factor per token
+  float* nrm_part = nullptr;  // [2][tc_norm_part_floats(D)]
+  float* nrm_r = nullptr;     // [B]
   void* tc_ws = nullptr;
   size_t tc_ws_bytes = 0;
   // tensor parallelism: buffers the peers read (one IPC-shared allocation per rank)
@@ -291,12 +298,29 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   const size_t wsb = h->tc_ws_bytes;
   constexpr int X2 = B2D_F16X2;
   uint16_t* const xn_lo = h->xn16 + (size_t)B * D;  // lo planes of this batch's operands
+  // Single GPU, fp16 weights: the RMSNorms after the O and the down projection are folded into
+  // the GEMMs (TcNorm) -- the projection emits x * gamma and slice sums of x^2, the next GEMM
+  // scales its product by the norm factor -- instead of a separate add_rmsnorm launch.
+  // B2D_NORM_FOLD=0 keeps the separate launches (read once).
+  static const bool fold_env = [] {
+    const char* e = std::getenv("B2D_NORM_FOLD");
+    return !(e && std::atoi(e) == 0);
+  }();
+  const bool fold = fold_env && !tpar && D % 128 == 0;
+  auto fold_into = [&](int l) {  // may the GEMMs of layer l (n_layers: the LM head) consume one
+    return fold && (l >= c.n_layers || h->layers[l].wdt == B2D_F16);
+  };
+  float* const part_o = h->nrm_part;  // slice sums after O (read by gate/up)
+  float* const part_down = h->nrm_part + align256(tc_norm_part_floats(D) * 4) / 4;  // after down
+  const float* pending = nullptr;  // slice sums the next QKV / LM head consumes (else normalized)
+  bool r_ok = fold;                // h->nrm_r holds this step's last norm factor per token
   B2D_TRY(embed_rmsnorm_f16(h->embed, tokens, h->x, h->layers[0].attn_norm, c.eps, h->xn16, xn_lo,
-                            D, B, s));
+                            fold ? h->nrm_r : nullptr, D, B, s));
   for (int l = 0; l < c.n_layers; ++l) {
     const Layer& L = h->layers[l];
     const float* next_norm = l + 1 < c.n_layers ? h->layers[l + 1].attn_norm : h->final_norm;
     const int wd = L.wdt;
+    const bool f = fold_into(l);
     // what each kernel prefetches into L2: the next weight-bearing kernel's matrices
     const Pf pf_o = pf_mat(L.wo, D, HQD, wd);
     const Pf pf_gate = pf_mat(wd == B2D_F16 ? L.wgate : L.wup, h->fl, D, wd);
@@ -306,12 +330,32 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
                            ? pf_mat(h->layers[l + 1].wqkv, h->qkv_l, D, h->layers[l + 1].wdt)
                            : (next_tokens ? pf_mat(h->lm_head, h->lm_rows, D, B2D_F16) : Pf{});
     // QKV (column-parallel)
-    B2D_TRY(tc_proj(h, wd, L.wqkv, L.sqkv, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
-                    h->qkv_l, nullptr, B, s, pf_o));
+    if (pending) {
+      TcNorm n;
+      n.part_in = pending;
+      n.r_out = h->nrm_r;
+      n.eps = c.eps;
+      B2D_TRY(tc_gemm_norm(X2, L.wqkv, nullptr, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv,
+                           h->qkv_l, nullptr, h->qkv_l, D, B, nullptr, nullptr, ws, wsb, s,
+                           pf_o.p, pf_o.n, n));
+      r_ok = true;
+    } else {
+      B2D_TRY(tc_proj(h, wd, L.wqkv, L.sqkv, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->qkv, h->qkv_l,
+                      h->qkv_l, nullptr, B, s, pf_o));
+      if (l > 0) r_ok = false;
+    }
     // RoPE + KV append + split-K attention -> hi/lo operand of the O projection
     B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s, pf_gate));
     // O projection (row-parallel) + residual, then RMSNorm(ffn) -> hi/lo
-    if (!tpar) {
+    if (f) {
+      TcNorm n;
+      n.gamma = L.ffn_norm;
+      n.planes = h->xn16;
+      n.part_out = part_o;
+      n.r_prev = r_ok ? h->nrm_r : nullptr;
+      B2D_TRY(tc_gemm_norm(X2, L.wo, nullptr, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D,
+                           nullptr, D, HQD, B, nullptr, nullptr, ws, wsb, s, pf_up.p, pf_up.n, n));
+    } else if (!tpar) {
       B2D_TRY(tc_proj(h, wd, L.wo, L.so, h->att16, HQD, B2D_EPI_ADD, B2D_F32, h->x, D, D,
                       nullptr, B, s, pf_up));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, L.ffn_norm, c.eps, h->xn16, xn_lo, B, D, s));
@@ -321,17 +365,39 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     }
     // gate/up SwiGLU (column-parallel) -> hi/lo.  fp16 weights: one dual-matrix GEMM; quantized
     // weights: the up projection into hid (fp32), then the gate projection times it.
-    if (wd == B2D_F16) {
+    if (f) {
+      TcNorm n;
+      n.part_in = part_o;
+      n.r_out = h->nrm_r;
+      n.eps = c.eps;
+      B2D_TRY(tc_gemm_norm(X2, L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, X2, h->h16, h->fl,
+                           nullptr, h->fl, D, B, nullptr, nullptr, ws, wsb, s, pf_down.p,
+                           pf_down.n, n));
+      r_ok = true;
+    } else if (wd == B2D_F16) {
       B2D_TRY(tc_gemm(X2, L.wgate, L.wup, h->xn16, D, B2D_EPI_SWIGLU, X2, h->h16, h->fl, nullptr,
                       h->fl, D, B, nullptr, nullptr, nullptr, 0, ws, wsb, s, pf_down.p, pf_down.n));
+      r_ok = false;
     } else {
       B2D_TRY(tc_proj(h, wd, L.wup, L.sup, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->hid, h->fl,
                       h->fl, nullptr, B, s, Pf{}));
       B2D_TRY(tc_proj(h, wd, L.wgate, L.sgate, h->xn16, D, B2D_EPI_SILU_MUL, X2, h->h16, h->fl,
                       h->fl, h->hid, B, s, pf_down));
+      r_ok = false;
     }
     // down (row-parallel) + residual, then the next RMSNorm -> hi/lo
-    if (!tpar) {
+    pending = nullptr;
+    if (f && fold_into(l + 1)) {
+      TcNorm n;
+      n.gamma = next_norm;
+      n.planes = h->xn16;
+      n.part_out = part_down;
+      n.r_prev = h->nrm_r;  // the gate/up GEMM's factor
+      B2D_TRY(tc_gemm_norm(X2, L.wdown, nullptr, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D,
+                           nullptr, D, h->fl, B, nullptr, nullptr, ws, wsb, s, pf_next.p,
+                           pf_next.n, n));
+      pending = part_down;
+    } else if (!tpar) {
       B2D_TRY(tc_proj(h, wd, L.wdown, L.sdown, h->h16, h->fl, B2D_EPI_ADD, B2D_F32, h->x, D, D,
                       nullptr, B, s, pf_next));
       B2D_TRY(add_rmsnorm_f16(h->x, nullptr, next_norm, c.eps, h->xn16, xn_lo, B, D, s));
@@ -343,7 +409,14 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
   // LM head (vocab-parallel) + argmax
   if (!next_tokens) return B2D_OK;
   const int offset = h->rank * h->lm_stride;
-  if (!tpar) {
+  if (pending) {
+    TcNorm n;
+    n.part_in = pending;
+    n.eps = c.eps;
+    B2D_TRY(tc_gemm_norm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
+                         nullptr, h->lm_rows, D, B, logits, next_tokens, ws, wsb, s, nullptr, 0,
+                         n));
+  } else if (!tpar) {
     B2D_TRY(tc_gemm(X2, h->lm_head, nullptr, h->xn16, D, B2D_EPI_ARGMAX, B2D_F32, nullptr, 0,
                     nullptr, h->lm_rows, D, B, logits, next_tokens, nullptr, 0, ws, wsb, s,
                     nullptr, 0));
@@ -581,6 +654,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
       (size_t)2 * B * 4,          (size_t)2 * B * c.max_blocks * 4,
       h->attn_ws_bytes,           h->am_ws_bytes,
       (size_t)2 * B * D * 2,      (size_t)2 * B * h->hq * c.head_dim * 2, (size_t)2 * B * h->fl * 2,
+      2 * align256(tc_norm_part_floats(D) * 4), (size_t)B * 4,
       h->tc_ws_bytes};
   size_t total = 0;
   for (size_t s : sizes) total += align256(s);
@@ -598,6 +672,7 @@ int b2d_decoder_create(const b2d_model_config* cfg, int tp_rank, int tp_size,
                     (void**)&h->pf_ctx,   (void**)&h->pf_table,
                     (void**)&h->attn_ws,  (void**)&h->am_ws,
                     (void**)&h->xn16,     (void**)&h->att16,    (void**)&h->h16,
+                    (void**)&h->nrm_part, (void**)&h->nrm_r,
                     (void**)&h->tc_ws};
   static_assert(sizeof(slots) / sizeof(slots[0]) == sizeof(sizes) / sizeof(sizes[0]),
                 "one slot per buffer size");

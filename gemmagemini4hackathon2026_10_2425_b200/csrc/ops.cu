@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(256) embed_rmsnorm_f16_kernel(const uint16_t* 
                                                                 const int* tokens, float* x,
                                                                 const float* gamma, float eps,
                                                                 uint16_t* out, uint16_t* out_lo,
-                                                                int D) {
+                                                                float* r_out, int D) {
   __shared__ float red[8];
   pdl_wait();
   const size_t tok = (size_t)tokens[blockIdx.x];
@@ -267,17 +267,19 @@ __global__ void __launch_bounds__(256) embed_rmsnorm_f16_kernel(const uint16_t* 
   float tot = 0.f;
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float scale = rsqrtf(tot / (float)D + eps);
+  if (r_out && threadIdx.x == 0) r_out[blockIdx.x] = scale;
   pdl_launch_dependents();
   for (int i = threadIdx.x; i < D; i += 256) store_f16_split(orow, lrow, i, xr[i] * scale * gamma[i]);
 }
 
+// r_out (optional): each row's norm factor rsqrt(mean(x^2) + eps).
 int embed_rmsnorm_f16(const uint16_t* E, const int* tokens, float* x, const float* gamma,
-                      float eps, uint16_t* out, uint16_t* out_lo, int D, int batch,
+                      float eps, uint16_t* out, uint16_t* out_lo, float* r_out, int D, int batch,
                       cudaStream_t stream) {
   if (!E || !tokens || !x || !gamma || !out) return B2D_ERR_NULL;
   if (D <= 0 || batch <= 0) return B2D_ERR_SHAPE;
   return launch_pdl(embed_rmsnorm_f16_kernel, dim3(batch), dim3(256), 0, stream, E, tokens, x,
-                    gamma, eps, out, out_lo, D);
+                    gamma, eps, out, out_lo, r_out, D);
 }
 
 }  // namespace b2d

@@ -90,8 +90,61 @@ struct Params {
   // adds; short chains keep each run to a few k-tiles.
   int chains;
   uint32_t tmem_cols;  // TMEM columns the CTA allocates (power of two >= 32)
+  // RMSNorm folded into a residual-add producer and the GEMM that consumes its output:
+  //   rmsnorm(x)[t] * gamma = r[t] * (x[t] * gamma),  r[t] = rsqrt(mean(x[t]^2) + eps)
+  // so W (rmsnorm(x) * gamma) = r[t] / e[t] * (W (x * gamma * e[t])) for any power of two e[t].
+  // Producer (ADD epilogue, nrm_gamma set): besides the new residual y it writes the hi / lo
+  // fp16 planes of y * gamma * e[t] to nrm_planes (lo at + batch * ldy), and to nrm_part_out
+  // the sum of y^2 over each 16-row slice, [32 tokens][M / 16], then e[32].  e[t] is the power
+  // of two at or below the last norm factor of token t (nrm_r_prev; 1 without it), which keeps
+  // the planes near unit scale.  Consumer (nrm_part_in set, fp16 weights): adds the slice sums
+  // in a fixed order, scales its product by r[t] / e[t] and, with nrm_r_out, records r[t].
+  const float* nrm_gamma;
+  uint16_t* nrm_planes;
+  float* nrm_part_out;
+  const float* nrm_r_prev;
+  const float* nrm_part_in;
+  float* nrm_r_out;
+  float nrm_eps;
 };
 constexpr int kMaxChains = 4;
+
+// The power of two at or below a positive normal float (1 for anything else).
+__device__ __forceinline__ float pow2_floor(float v) {
+  const float e = __int_as_float(__float_as_int(v) & 0x7f800000);
+  return v > 0.f && e > 0.f && e < INFINITY ? e : 1.f;
+}
+
+// Barrier among the four epilogue warps (128 threads), leaving the other warps free.
+__device__ __forceinline__ void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Folded RMSNorm, producer: once the epilogue threads have put y^2 of their owned rows into
+// sq ([token][owned row], zero for rows past M), each 16-row slice's sum per token, added in
+// row order, goes to nrm_part_out[t][slice]; owned slice ls is slice gs0 + ls * gs_step of M.
+// One CTA (write_e) also records e[t] after the sums.
+__device__ __forceinline__ void nrm_slice_sums(const Params& p, const float* sq,
+                                               const float* nrm_e, int own_rows, int gs0,
+                                               int gs_step, int etid, bool write_e) {
+  epi_bar_sync();
+  const int nsl = own_rows / 16, S = p.M / 16;
+  for (int i = etid; i < nsl * p.batch; i += THREADS) {
+    const int t = i / nsl, ls = i - t * nsl;
+    const int gs = gs0 + ls * gs_step;
+    if (gs >= S) continue;
+    const float4* src = reinterpret_cast<const float4*>(sq + t * own_rows + ls * 16);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 u = src[j];
+      sum += u.x;
+      sum += u.y;
+      sum += u.z;
+      sum += u.w;
+    }
+    p.nrm_part_out[(size_t)t * S + gs] = sum;
+  }
+  if (write_e && etid < p.batch) p.nrm_part_out[(size_t)32 * S + etid] = nrm_e[etid];
+}
 
 // y[yi] = v into y, or into every copy in p.ys
 template <typename P>
@@ -281,6 +334,8 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   __shared__ bool is_last;
   __shared__ float am_v[4][N];
   __shared__ int am_i[4][N];
+  __shared__ float nrm_s[N];  // folded RMSNorm, consumer: r[t] / e[t]
+  __shared__ float nrm_e[N];  // folded RMSNorm, producer: e[t]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m_tile = blockIdx.x, split = blockIdx.y;
@@ -550,6 +605,38 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         mbar_arrive(&raw_empty[rs]);
       }
     }
+  } else if (!QUANT && (warp == 2 || warp == 3) && p.nrm_part_in) {
+    // ---------------- folded RMSNorm: the per-token factor, during the main loop ----------------
+    // Two threads per token each add half of the producer's slice sums (four interleaved fp32
+    // sums, combined in a fixed order), then r = rsqrt(sum / K + eps).
+    pdl_wait();  // the slice sums come from the previous kernel
+    const int q = tid - 64, t = q >> 1, half = q & 1;
+    const int S = p.K / 16;
+    float ssum = 0.f;
+    if (t < p.batch) {
+      const float4* src =
+          reinterpret_cast<const float4*>(p.nrm_part_in + (size_t)t * S) + half * (S / 8);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < S / 8; ++i) {
+        const float4 u = src[i];
+        a0 += u.x;
+        a1 += u.y;
+        a2 += u.z;
+        a3 += u.w;
+      }
+      ssum = (a0 + a1) + (a2 + a3);
+    }
+    ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);  // both halves: the same sum
+    if (half == 0 && t < N) {
+      float sc = 1.f;
+      if (t < p.batch) {
+        const float rn = rsqrtf(ssum / (float)p.K + p.nrm_eps);
+        sc = rn / p.nrm_part_in[(size_t)32 * S + t];
+        if (p.nrm_r_out && m_tile == 0 && split == 0) p.nrm_r_out[t] = rn;
+      }
+      nrm_s[t] = sc;
+    }
   }
   __syncwarp();
 
@@ -581,6 +668,13 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
         }
       }
     }
+    if (!QUANT && p.nrm_part_in) {  // folded RMSNorm: the product times r[t] / e[t]
+#pragma unroll
+      for (int t = 0; t < N; ++t) {
+        acc[t] *= nrm_s[t];
+        if constexpr (DUAL) acc2[t] *= nrm_s[t];
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -592,6 +686,11 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
   const int r = (warp & 3) * 32 + lane;       // row within the tile (epilogue warps)
   const int etid = (warp - EPI0) * 32 + lane;  // 0..127 on epilogue warps
   const int row = m0 + r;
+  // folded RMSNorm, producer side (ADD epilogue): CTA-uniform; y^2 per (token, owned row) is
+  // staged in the operand ring, idle once the accumulator is complete
+  constexpr bool EMIT = !DUAL && !ARGMAX;
+  const bool emit = EMIT && p.nrm_gamma != nullptr && p.epi == B2D_EPI_ADD;
+  float* sq = reinterpret_cast<float*>(smem);
 
   if (p.k_splits > 1) {
     // Split-K through the thread-block cluster: the k_splits CTAs of this row tile form one
@@ -627,6 +726,7 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     // what those items read from global memory while the barrier completes
     constexpr int MAXQ = N / 8;  // items per thread (k_splits >= 2)
     float yv[DUAL ? 1 : MAXQ][4];
+    float gv[EMIT ? MAXQ : 1];  // folded RMSNorm: gamma of each item's row
     pdl_wait();
     pdl_launch_dependents();
     const int nq = own_rows * (N / 4);
@@ -645,9 +745,12 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             yv[k][j] = p.epi == B2D_EPI_ADD ? load_y(p, yi) : p.aux[yi];
           }
         }
+        if constexpr (EMIT) gv[k] = emit && v < nq && grow < p.M ? p.nrm_gamma[grow] : 0.f;
       }
     }
-    cl.sync();  // every partial row has reached its owner
+    if (emit && ok && epi_warp && etid < N)
+      nrm_e[etid] = etid < p.batch && p.nrm_r_prev ? pow2_floor(p.nrm_r_prev[etid]) : 1.f;
+    cl.sync();  // every partial row has reached its owner (and nrm_e is visible)
     if (ok && epi_warp) {
 #pragma unroll
       for (int k = 0; k < MAXQ; ++k) {
@@ -670,7 +773,13 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             a2.w += u2.w;
           }
         }
-        if (grow >= p.M) continue;
+        if (grow >= p.M) {
+          if (emit) {  // rows past M add nothing to their slice's sum
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sq[(t0 + j) * own_rows + lr] = 0.f;
+          }
+          continue;
+        }
         const float av[4] = {a.x, a.y, a.z, a.w}, a2v[4] = {a2.x, a2.y, a2.z, a2.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -687,8 +796,18 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
             else if (p.epi == B2D_EPI_SILU_MUL) y = silu(y) * yv[k][j];
           }
           store_y(p, yi, y);
+          if constexpr (EMIT) {
+            if (emit) {
+              store_f16_split(p.nrm_planes, p.nrm_planes + (size_t)p.batch * p.ldy, yi,
+                              y * gv[k] * nrm_e[t]);
+              sq[t * own_rows + lr] = y * y;
+            }
+          }
         }
       }
+      if (emit)
+        nrm_slice_sums(p, sq, nrm_e, own_rows, m_tile * (BM / 16) + rank, ks, etid,
+                       m_tile == 0 && rank == 0);
     }
     return;
   }
@@ -736,6 +855,30 @@ __global__ void __launch_bounds__(threads_for(QUANT), 1)
     }
     if (tid == 0) *p.am_counter = 0u;
   } else {
+    if constexpr (EMIT) {
+      if (emit) {
+        if (etid < N)
+          nrm_e[etid] = etid < p.batch && p.nrm_r_prev ? pow2_floor(p.nrm_r_prev[etid]) : 1.f;
+        epi_bar_sync();
+        const float g = row < p.M ? p.nrm_gamma[row] : 0.f;
+#pragma unroll
+        for (int t = 0; t < N; ++t) {
+          if (t >= p.batch) break;
+          float sqv = 0.f;
+          if (row < p.M) {
+            const size_t yi = (size_t)t * p.ldy + row;
+            const float v = acc[t] + load_y(p, yi);
+            store_y(p, yi, v);
+            store_f16_split(p.nrm_planes, p.nrm_planes + (size_t)p.batch * p.ldy, yi,
+                            v * g * nrm_e[t]);
+            sqv = v * v;
+          }
+          sq[t * BM + r] = sqv;
+        }
+        nrm_slice_sums(p, sq, nrm_e, BM, m_tile * (BM / 16), 1, etid, m_tile == 0);
+        return;
+      }
+    }
     if (row >= p.M) return;
 #pragma unroll
     for (int t = 0; t < N; ++t) {
@@ -1097,6 +1240,39 @@ int tc_gemm(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t
                           workspace_bytes));
   c.prm.pf = pf;
   c.prm.pf_bytes = pf_bytes;
+  return tc_gemm_launch(c, stream);
+}
+
+// tc_gemm with the RMSNorm of its input and / or of its output folded in (TcNorm).  fp16 weights
+// only.  Producer: ADD epilogue into fp32 y, M % 16 == 0.  Consumer: K % 128 == 0, part_in
+// 16-byte aligned.
+int tc_gemm_norm(int x_dtype, const uint16_t* W, const uint16_t* W_up, const uint16_t* X,
+                 int ldx, int epilogue, int y_dtype, void* y, int ldy, const float* aux, int M,
+                 int K, int batch, float* logits, int* tokens, void* workspace,
+                 size_t workspace_bytes, cudaStream_t stream, const void* pf, size_t pf_bytes,
+                 const TcNorm& nrm) {
+  if (nrm.gamma) {
+    if (!nrm.planes || !nrm.part_out) return B2D_ERR_NULL;
+    if (epilogue != B2D_EPI_ADD || y_dtype != B2D_F32) return B2D_ERR_UNSUPPORTED;
+    if (M % 16) return B2D_ERR_SHAPE;
+  }
+  if (nrm.part_in) {
+    if (K % 128) return B2D_ERR_SHAPE;
+    if (!aligned16(nrm.part_in)) return B2D_ERR_ALIGN;
+  }
+  TcCall c;
+  B2D_TRY(tc_gemm_prepare(&c, x_dtype, W, W_up, X, ldx, epilogue, y_dtype, y, ldy, aux, M, K,
+                          batch, logits, tokens, nullptr, 0, workspace, workspace_bytes));
+  tc::Params& p = c.prm;
+  p.pf = pf;
+  p.pf_bytes = pf_bytes;
+  p.nrm_gamma = nrm.gamma;
+  p.nrm_planes = nrm.planes;
+  p.nrm_part_out = nrm.part_out;
+  p.nrm_r_prev = nrm.r_prev;
+  p.nrm_part_in = nrm.part_in;
+  p.nrm_r_out = nrm.r_out;
+  p.nrm_eps = nrm.eps;
   return tc_gemm_launch(c, stream);
 }
 
