@@ -37,9 +37,10 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # DRAM bytes per launch of the two kernel families, from one ncu capture of each
 # (dram__bytes_read.sum + dram__bytes_write.sum): paged_attn_tc_kernel<64,4> on one config-5
-# layer, and tc_gemm_kernel<32, SWIGLU> on the config-5 gate/up projection
-ATTN_C5_TRAFFIC = 160_088_832 + 3_824_384
-GATEUP_TRAFFIC = 67_329_280 + 683_264
+# layer (1024-key chunks), and tc_gemm_kernel<32, SWIGLU, hi/lo planes> on the config-5 gate/up
+# projection (--op c5_attn_hd64 / --op c5_gateup_tc, ncu --set full, one launch each)
+ATTN_C5_TRAFFIC = 160_069_120 + 3_772_416
+GATEUP_TRAFFIC = 67_438_592 + 913_408
 
 
 def peaks() -> tuple[float, str]:

@@ -53,9 +53,6 @@ struct AttnParams {
   unsigned int* counters;  // [B][Hkv]
   float* partials;         // [B][Hkv][max_chunks][G][HD + 2]
   int* err;                // error word (a bounded wait gave up)
-  // the next kernel's weights, pulled into L2 by this kernel's tail (nullptr: none)
-  const void* pf;
-  unsigned long long pf_bytes;
 };
 
 __device__ __forceinline__ float load_qkv(const AttnParams& p, size_t i) {
@@ -512,12 +509,8 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
   const int n = pos + 1;
   const int start = (p.window > 0 && n > p.window) ? n - p.window : 0;
   const int first_c = start / p.chunk, last_c = (n - 1) / p.chunk;
-  if (pos < 0 || pos >= p.max_ctx || c < first_c || c > last_c) {
-    // no keys here (or outside the caller's contract: output untouched); this CTA's share of
-    // the next kernel's weights still goes to L2
-    if (threadIdx.x == 0) l2_prefetch_share(p.pf, p.pf_bytes);
-    return;
-  }
+  // no keys here (or outside the caller's contract: output untouched)
+  if (pos < 0 || pos >= p.max_ctx || c < first_c || c > last_c) return;
   const int tok_lo = max(c * p.chunk, start);
   const int tok_hi = min((c + 1) * p.chunk, n);
   const int nact = last_c - first_c + 1;
@@ -733,8 +726,6 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tc_kernel(const __gri
     if (lane == 0)  // let this warp's copies in flight land before the CTA exits
       for (int k = 0; k < issued; ++k) mbar_wait(&full_bar[warp][k % SW], (k / SW) & 1, p.err, 1);
     cta_failed = 1;
-  } else if (tid == 0) {
-    l2_prefetch_share(p.pf, p.pf_bytes);  // this CTA's pages are consumed: next weights to L2
   }
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
@@ -960,7 +951,7 @@ int paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages, ui
                       const float* inv_freq, int n_heads, int n_kv_heads, int head_dim,
                       int batch, int max_ctx, float scale, int window, int append, void* out,
                       int out_dtype, int ldout, void* workspace, size_t workspace_bytes,
-                      cudaStream_t stream, const void* pf = nullptr, size_t pf_bytes = 0) {
+                      cudaStream_t stream) {
   if (!qkv || !k_pages || !v_pages || !block_table || !ctx_lens || !out) return B2D_ERR_NULL;
   if (append && !inv_freq) return B2D_ERR_NULL;
   if (batch <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || max_ctx <= 0 ||
@@ -998,8 +989,6 @@ int paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages, ui
   prm.out_lo = out_dtype == B2D_F16X2 ? static_cast<uint16_t*>(out) + (size_t)batch * ldout : nullptr;
   prm.ldout = ldout;
   prm.max_ctx = max_ctx;
-  prm.pf = pf;
-  prm.pf_bytes = pf_bytes;
   prm.chunk = attn_chunk_tokens(batch, n_kv_heads, max_ctx);
   prm.max_chunks = (max_ctx + prm.chunk - 1) / prm.chunk;
   char* ws = static_cast<char*>(workspace);

@@ -66,7 +66,7 @@ int tp_argmax_gather(const float* const*, const int* const*, uint32_t* const*, u
 size_t paged_attn_workspace_bytes(int, int, int, int, int);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
-                      void*, size_t, cudaStream_t, const void*, size_t);
+                      void*, size_t, cudaStream_t);
 
 }  // namespace b2d
 
@@ -297,7 +297,7 @@ int b2d_paged_decode_attn(void* qkv, int qkv_dtype, int ldqkv, uint16_t* k_pages
   return paged_decode_attn(qkv, qkv_dtype, ldqkv, k_pages, v_pages, block_table, max_blocks,
                            n_blocks, ctx_lens, inv_freq, n_heads, n_kv_heads, head_dim, batch,
                            max_ctx, scale, window, append, out, out_dtype, ldout, workspace,
-                           workspace_bytes, S(stream), nullptr, 0);
+                           workspace_bytes, S(stream));
 }
 
 }  // extern "C"

@@ -43,7 +43,7 @@ size_t paged_attn_workspace_bytes(int, int, int, int, int);
 size_t attn_ws_header_bytes(int batch, int n_kv_heads);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
-                      void*, size_t, cudaStream_t, const void* pf, size_t pf_bytes);
+                      void*, size_t, cudaStream_t);
 int rope_kv_append(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                    const float*, int, int, int, int, cudaStream_t);
 int add_rmsnorm_f16(float*, const float*, const float*, float, uint16_t*, uint16_t*, int, int,
@@ -272,7 +272,7 @@ static int tp_argmax(b2d_decoder* h, int B, int* next_tokens, cudaStream_t s) {
 // attention then only reads the pages.
 static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
                            const int* block_table, int B, bool prefill, void* out, int out_dtype,
-                           cudaStream_t s, Pf pf = Pf{}) {
+                           cudaStream_t s) {
   const b2d_model_config& c = h->cfg;
   const int HD = c.head_dim;
   if (prefill)
@@ -281,7 +281,7 @@ static int layer_attention(b2d_decoder* h, const Layer& L, const int* ctx_lens,
   return paged_decode_attn(h->qkv, B2D_F32, h->qkv_l, L.k_pages, L.v_pages, block_table,
                            c.max_blocks, c.n_blocks, ctx_lens, h->invf, h->hq, h->hk, HD, B,
                            c.max_ctx, 0.f, 0, prefill ? 0 : 1, out, out_dtype, h->hq * HD,
-                           h->attn_ws, h->attn_ws_bytes, s, pf.p, pf.n);
+                           h->attn_ws, h->attn_ws_bytes, s);
 }
 
 // Tensor-core step (batch >= kTcMinBatch): every projection's activation operand enters as
@@ -323,8 +323,8 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
     const bool f = fold_into(l);
     // what each kernel prefetches into L2: the next weight-bearing kernel's matrices
     const Pf pf_o = pf_mat(L.wo, D, HQD, wd);
-    const Pf pf_gate = pf_mat(wd == B2D_F16 ? L.wgate : L.wup, h->fl, D, wd);
-    const Pf pf_up = pf_mat(wd == B2D_F16 ? L.wup : L.wgate, h->fl, D, wd);
+    const Pf pf_up = pf_mat(L.wup, h->fl, D, wd);
+    const Pf pf_gate = pf_mat(L.wgate, h->fl, D, wd);
     const Pf pf_down = pf_mat(L.wdown, D, h->fl, wd);
     const Pf pf_next = l + 1 < c.n_layers
                            ? pf_mat(h->layers[l + 1].wqkv, h->qkv_l, D, h->layers[l + 1].wdt)
@@ -345,7 +345,7 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
       if (l > 0) r_ok = false;
     }
     // RoPE + KV append + split-K attention -> hi/lo operand of the O projection
-    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s, pf_gate));
+    B2D_TRY(layer_attention(h, L, ctx_lens, block_table, B, prefill, h->att16, X2, s));
     // O projection (row-parallel) + residual, then RMSNorm(ffn) -> hi/lo
     if (f) {
       TcNorm n;
@@ -380,7 +380,7 @@ static int enqueue_step_tc(b2d_decoder* h, const int* tokens, const int* ctx_len
       r_ok = false;
     } else {
       B2D_TRY(tc_proj(h, wd, L.wup, L.sup, h->xn16, D, B2D_EPI_STORE, B2D_F32, h->hid, h->fl,
-                      h->fl, nullptr, B, s, Pf{}));
+                      h->fl, nullptr, B, s, pf_gate));
       B2D_TRY(tc_proj(h, wd, L.wgate, L.sgate, h->xn16, D, B2D_EPI_SILU_MUL, X2, h->h16, h->fl,
                       h->fl, h->hid, B, s, pf_down));
       r_ok = false;

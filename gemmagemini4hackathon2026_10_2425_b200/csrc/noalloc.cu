@@ -29,7 +29,7 @@ size_t paged_attn_workspace_bytes(int, int, int, int, int);
 size_t attn_ws_header_bytes(int batch, int n_kv_heads);
 int paged_decode_attn(void*, int, int, uint16_t*, uint16_t*, const int*, int, int, const int*,
                       const float*, int, int, int, int, int, float, int, int, void*, int, int,
-                      void*, size_t, cudaStream_t, const void*, size_t);
+                      void*, size_t, cudaStream_t);
 }  // namespace b2d
 
 using namespace b2d;
@@ -92,7 +92,7 @@ int b2d_paged_decode_attn_noalloc(void* qkv, int qkv_dtype, int ldqkv, uint16_t*
   return paged_decode_attn(qkv, qkv_dtype, ldqkv, k_pages, v_pages, block_table, max_blocks,
                            n_blocks, ctx_lens, inv_freq, n_heads, n_kv_heads, head_dim, batch,
                            max_ctx, scale, window, append, out, out_dtype, ldout, scratch,
-                           kNoAllocScratchBytes, s, nullptr, 0);
+                           kNoAllocScratchBytes, s);
 }
 
 int b2d_paged_decode_attn_noalloc_error(void) {
