@@ -39,7 +39,7 @@ FALLBACK_HBM = 6650.0  # GB/s, used only when MEASURED_PEAKS.json is absent
 # (dram__bytes_read.sum + dram__bytes_write.sum): paged_attn_tc_kernel<64,4> on one config-5
 # layer (1024-key chunks), and tc_gemm_kernel<32, SWIGLU, hi/lo planes> on the config-5 gate/up
 # projection (--op c5_attn_hd64 / --op c5_gateup_tc, ncu --set full, one launch each)
-ATTN_C5_TRAFFIC = 160_069_120 + 3_772_416
+ATTN_C5_TRAFFIC = 160_049_152 + 3_264_512
 GATEUP_TRAFFIC = 67_438_592 + 913_408
 
 
