@@ -283,8 +283,9 @@ def op_benchmarks(peak: float, only: str | None = None, iters: int | None = None
     def copies(nbytes):  # enough distinct operand copies to exceed 2x L2
         return max(1, -(-(2 * L2) // nbytes))
 
-    def want(key):  # key selected, or a prefix of the selected key (outer loops)
-        return only is None or key.startswith(only) or only.startswith(key)
+    def want(key):  # key selected, under the selected prefix, or an outer loop of the selected key
+        # (matched on whole "_"-separated parts: "..._b1" does not select "..._b16")
+        return only is None or key == only or key.startswith(only + "_") or only.startswith(key + "_")
 
     def nit(default):
         return iters if iters is not None else default

@@ -390,46 +390,68 @@ __device__ void stage_columns(const MmaGemvParams& p, uint16_t* xs, int XS, floa
   // element order of a staged group of 8: natural, or (0,4)(1,5)(2,6)(3,7) for 4-bit weights
   constexpr bool P4 = WT == MW_Q4;
   constexpr int perm[8] = {0, P4 ? 4 : 1, P4 ? 1 : 2, P4 ? 5 : 3, P4 ? 2 : 4, P4 ? 6 : 5, P4 ? 3 : 6, 7};
+  if (!p.lo) {
+    // fp16 activations, no norm: copied (reordered for 4-bit weights).  Staging reads what the
+    // previous kernel wrote, so it is on the critical path: each thread issues the loads of TC
+    // tokens of one 8-element group before storing any of them (one memory latency per batch
+    // of tokens, not one per token).
+    constexpr int TC = 4;
+    for (int i = tid; i < n8; i += nthr) {
+#pragma unroll
+      for (int t0 = 0; t0 < kMaxTok; t0 += TC) {
+        if (t0 >= nb) break;
+        uint4 x[TC];
+#pragma unroll
+        for (int u = 0; u < TC; ++u)
+          if (t0 + u < nb)
+            x[u] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.x) +
+                                                   (size_t)(t0 + u) * p.ldx + 8 * i);
+#pragma unroll
+        for (int u = 0; u < TC; ++u) {
+          if (t0 + u >= nb) break;
+          uint32_t hi[4];
+          if constexpr (P4) {
+            hi[0] = __byte_perm(x[u].x, x[u].z, 0x5410);  // (x0, x4)
+            hi[1] = __byte_perm(x[u].x, x[u].z, 0x7632);  // (x1, x5)
+            hi[2] = __byte_perm(x[u].y, x[u].w, 0x5410);  // (x2, x6)
+            hi[3] = __byte_perm(x[u].y, x[u].w, 0x7632);  // (x3, x7)
+          } else {
+            hi[0] = x[u].x, hi[1] = x[u].y, hi[2] = x[u].z, hi[3] = x[u].w;
+          }
+          *reinterpret_cast<uint4*>(xs + (size_t)(t0 + u) * XS + 8 * i) =
+              make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        }
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  // hi + lo columns of x * norm * gamma * 2^e
   for (int tok = 0; tok < nb; ++tok) {
     for (int i = tid; i < n8; i += nthr) {
       uint32_t hi[4], lo[4];
-      if (p.lo) {
-        float v[8];
-        load_x8(p, tok, i, v);
-        const float ns = tok_norm[tok], f = tok_pow[tok];
+      float v[8];
+      load_x8(p, tok, i, v);
+      const float ns = tok_norm[tok], f = tok_pow[tok];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint16_t h[2], l[2];
+      for (int q = 0; q < 4; ++q) {
+        uint16_t h[2], l[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int e = perm[2 * q + u];
-            float xv = v[e] * ns;
-            if (p.gamma) xv *= __ldg(p.gamma + 8 * i + e);
-            xv *= f;
-            h[u] = f2h(xv);
-            l[u] = f2h(xv - h2f(h[u]));
-          }
-          hi[q] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-          lo[q] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
+        for (int u = 0; u < 2; ++u) {
+          const int e = perm[2 * q + u];
+          float xv = v[e] * ns;
+          if (p.gamma) xv *= __ldg(p.gamma + 8 * i + e);
+          xv *= f;
+          h[u] = f2h(xv);
+          l[u] = f2h(xv - h2f(h[u]));
         }
-        *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok) * XS + 8 * i) =
-            make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok + 1) * XS + 8 * i) =
-            make_uint4(lo[0], lo[1], lo[2], lo[3]);
-      } else {  // fp16 activations, no norm: copied (reordered for 4-bit weights)
-        const uint4 u = *reinterpret_cast<const uint4*>(
-            reinterpret_cast<const uint16_t*>(p.x) + (size_t)tok * p.ldx + 8 * i);
-        if constexpr (P4) {
-          hi[0] = __byte_perm(u.x, u.z, 0x5410);  // (x0, x4)
-          hi[1] = __byte_perm(u.x, u.z, 0x7632);  // (x1, x5)
-          hi[2] = __byte_perm(u.y, u.w, 0x5410);  // (x2, x6)
-          hi[3] = __byte_perm(u.y, u.w, 0x7632);  // (x3, x7)
-        } else {
-          hi[0] = u.x, hi[1] = u.y, hi[2] = u.z, hi[3] = u.w;
-        }
-        *reinterpret_cast<uint4*>(xs + (size_t)tok * XS + 8 * i) =
-            make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        hi[q] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+        lo[q] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
       }
+      *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok) * XS + 8 * i) =
+          make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok + 1) * XS + 8 * i) =
+          make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
   }
   __syncthreads();
