@@ -335,7 +335,42 @@ __device__ __forceinline__ void load_x8(const MmaGemvParams& p, int tok, int i, 
   }
 }
 
+// gamma[8i .. 8i + 8), eight independent loads (all ones without gamma: multiplying by them is
+// exact).
+__device__ __forceinline__ void load_gamma8(const MmaGemvParams& p, int i, float (&g)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) g[e] = p.gamma ? __ldg(p.gamma + 8 * i + e) : 1.f;
+}
+
+// One 8-element group of a token as hi and lo fp16 columns: x * ns * gamma * f, in the staged
+// element order (natural, or (0,4)(1,5)(2,6)(3,7) for 4-bit weights).
+template <bool P4>
+__device__ __forceinline__ void store_hilo8(uint16_t* xs, int XS, int tok, int i, const float (&v)[8],
+                                            const float (&g)[8], float ns, float f) {
+  constexpr int perm[8] = {0, P4 ? 4 : 1, P4 ? 1 : 2, P4 ? 5 : 3, P4 ? 2 : 4, P4 ? 6 : 5, P4 ? 3 : 6, 7};
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint16_t h[2], l[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int e = perm[2 * q + u];
+      float xv = v[e] * ns;
+      xv *= g[e];
+      xv *= f;
+      h[u] = f2h(xv);
+      l[u] = f2h(xv - h2f(h[u]));
+    }
+    hi[q] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+    lo[q] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
+  }
+  *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok) * XS + 8 * i) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok + 1) * XS + 8 * i) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
 // Stage the activation columns (see the file comment).  tok_inv[t] undoes the token's scale.
+// Staging reads what the previous kernel wrote, so it is on the critical path: loads of
+// several tokens of a group are issued before the first is used.
 template <int WT>
 __device__ void stage_columns(const MmaGemvParams& p, uint16_t* xs, int XS, float* tok_inv) {
   __shared__ float st_ss[kMaxWarps][kMaxTok], st_mx[kMaxWarps][kMaxTok];
@@ -343,23 +378,40 @@ __device__ void stage_columns(const MmaGemvParams& p, uint16_t* xs, int XS, floa
   const int tid = threadIdx.x, nthr = blockDim.x, warp = tid >> 5, lane = tid & 31;
   const int n8 = p.K / 8, nb = p.nb;
   if (p.lo) {
-    for (int tok = 0; tok < nb; ++tok) {
-      float ss = 0.f, mx = 0.f;
+    // per token: the sum of squares and the largest |x * gamma|; two tokens per pass over the
+    // thread's groups, their loads (and gamma's) issued together
+    for (int t0 = 0; t0 < nb; t0 += 2) {
+      const bool two = t0 + 1 < nb;
+      float ss0 = 0.f, mx0 = 0.f, ss1 = 0.f, mx1 = 0.f;
       for (int i = tid; i < n8; i += nthr) {
-        float v[8];
-        load_x8(p, tok, i, v);
+        float v0[8], v1[8], g[8];
+        load_x8(p, t0, i, v0);
+        if (two) load_x8(p, t0 + 1, i, v1);
+        load_gamma8(p, i, g);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          ss = fmaf(v[e], v[e], ss);
-          const float gv = p.gamma ? v[e] * __ldg(p.gamma + 8 * i + e) : v[e];
-          mx = fmaxf(mx, fabsf(gv));
+          ss0 = fmaf(v0[e], v0[e], ss0);
+          mx0 = fmaxf(mx0, fabsf(v0[e] * g[e]));
+        }
+        if (two) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            ss1 = fmaf(v1[e], v1[e], ss1);
+            mx1 = fmaxf(mx1, fabsf(v1[e] * g[e]));
+          }
         }
       }
-      ss = warp_sum(ss);
-      mx = warp_max(mx);
+      ss0 = warp_sum(ss0);
+      mx0 = warp_max(mx0);
+      ss1 = warp_sum(ss1);
+      mx1 = warp_max(mx1);
       if (lane == 0) {
-        st_ss[warp][tok] = ss;
-        st_mx[warp][tok] = mx;
+        st_ss[warp][t0] = ss0;
+        st_mx[warp][t0] = mx0;
+        if (two) {
+          st_ss[warp][t0 + 1] = ss1;
+          st_mx[warp][t0 + 1] = mx1;
+        }
       }
     }
     __syncthreads();
@@ -389,7 +441,6 @@ __device__ void stage_columns(const MmaGemvParams& p, uint16_t* xs, int XS, floa
   }
   // element order of a staged group of 8: natural, or (0,4)(1,5)(2,6)(3,7) for 4-bit weights
   constexpr bool P4 = WT == MW_Q4;
-  constexpr int perm[8] = {0, P4 ? 4 : 1, P4 ? 1 : 2, P4 ? 5 : 3, P4 ? 2 : 4, P4 ? 6 : 5, P4 ? 3 : 6, 7};
   if (!p.lo) {
     // fp16 activations, no norm: copied (reordered for 4-bit weights).  Staging reads what the
     // previous kernel wrote, so it is on the critical path: each thread issues the loads of TC
@@ -426,32 +477,16 @@ __device__ void stage_columns(const MmaGemvParams& p, uint16_t* xs, int XS, floa
     __syncthreads();
     return;
   }
-  // hi + lo columns of x * norm * gamma * 2^e
-  for (int tok = 0; tok < nb; ++tok) {
+  // hi + lo columns of x * norm * gamma * 2^e, two tokens per pass as above
+  for (int t0 = 0; t0 < nb; t0 += 2) {
+    const bool two = t0 + 1 < nb;
     for (int i = tid; i < n8; i += nthr) {
-      uint32_t hi[4], lo[4];
-      float v[8];
-      load_x8(p, tok, i, v);
-      const float ns = tok_norm[tok], f = tok_pow[tok];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint16_t h[2], l[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int e = perm[2 * q + u];
-          float xv = v[e] * ns;
-          if (p.gamma) xv *= __ldg(p.gamma + 8 * i + e);
-          xv *= f;
-          h[u] = f2h(xv);
-          l[u] = f2h(xv - h2f(h[u]));
-        }
-        hi[q] = (uint32_t)h[0] | ((uint32_t)h[1] << 16);
-        lo[q] = (uint32_t)l[0] | ((uint32_t)l[1] << 16);
-      }
-      *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok) * XS + 8 * i) =
-          make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(xs + (size_t)(2 * tok + 1) * XS + 8 * i) =
-          make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      float v0[8], v1[8], g[8];
+      load_x8(p, t0, i, v0);
+      if (two) load_x8(p, t0 + 1, i, v1);
+      load_gamma8(p, i, g);
+      store_hilo8<P4>(xs, XS, t0, i, v0, g, tok_norm[t0], tok_pow[t0]);
+      if (two) store_hilo8<P4>(xs, XS, t0 + 1, i, v1, g, tok_norm[t0 + 1], tok_pow[t0 + 1]);
     }
   }
   __syncthreads();
